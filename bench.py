@@ -1,0 +1,466 @@
+"""Headline benchmark: post_attn_mlp at Llama-3-8B widths on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode step's MLP half: 32 stacked post_attn_mlp layers
+(hidden 4096, intermediate 14336, bf16, independent seeded weights), replayed
+as one CUDA graph.  The metric is microseconds per layer at M=1 (M=8 is
+reported beside it) and the HBM bandwidth that implies, against the measured
+copy roof.  With N>1 GPUs (torchrun) the same 32-layer stack runs tensor-
+parallel: gate/up column-sharded, down row-sharded, one NCCL allreduce per
+layer (strong scaling: the total work is fixed).
+
+Rank 0 prints ONE JSON line.  --impl reference times the reference's CPU
+formulation of the same layer (the oracle port of reference.py, numpy fp32) on
+the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I = 4096, 14336
+LAYERS = 32
+EPS = 1e-5
+PUBLISHED_US = {1: 1570.0, 8: 1621.0}  # reference bf16 post_attn_mlp, RTX 4070 Laptop
+METRIC = "post_attn_mlp us/layer at M=1 (Llama-3-8B widths, 32-layer CUDA graph), HBM GB/s vs measured peak"
+
+
+def layer_bytes(m: int, h: int = H, i: int = I, world: int = 1) -> int:
+    """Algorithmic HBM bytes of one layer on one rank: weights once, hidden in,
+    out, norm weight.  Intermediates stay in L2 and are not counted."""
+    return (2 * i * h + h * i) * 2 // world + 3 * m * h * 2 if m else 0
+
+
+def gate_up_launch_bytes(m: int, world: int = 1) -> int:
+    """Algorithmic bytes of one gate/up-kernel launch: weight, hidden, norm weight, mid."""
+    return 2 * I * H * 2 // world + m * H * 2 + H * 2 + m * (I // world) * 2
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def committed_traffic() -> dict:
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.lines: list[tuple[float, str]] = []
+        self.proc = None
+        self.thread = None
+        self.window = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        time.sleep(0.3)
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def mark(self, t0: float, t1: float) -> None:
+        """Restrict the summary to samples taken in [t0, t1] (the timed region)."""
+        self.window = (t0, t1)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        lines = self.lines
+        if self.window is not None:
+            inside = [ln for t, ln in lines if self.window[0] <= t <= self.window[1] + 0.15]
+            lines = inside if inside else [ln for _, ln in lines]
+        else:
+            lines = [ln for _, ln in lines]
+        for ln in lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU leg
+def cpu_layer_sample(layers: int, m: int, seed: int = 0):
+    """Seeded fp32 copies (bf16-rounded values) of `layers` Llama-3-8B MLP layers for the CPU leg."""
+    from oracle import fd_oracle as O
+
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(layers):
+        nw = O.round_bf16(1 + 0.1 * rng.standard_normal(H, dtype=np.float32))
+        wgu = O.round_bf16(rng.standard_normal((2 * I, H), dtype=np.float32) * np.float32(0.02))
+        wd = O.round_bf16(rng.standard_normal((H, I), dtype=np.float32) * np.float32(0.02))
+        out.append((nw, wgu, wd))
+    x = O.round_bf16(rng.standard_normal((m, H), dtype=np.float32))
+    return x, out
+
+
+def cpu_time_layers(x, layers, budget_s: float, min_evals: int, max_evals: int | None = None):
+    """Time the oracle's post_attn_mlp per layer; returns (us/layer, evals, threads)."""
+    from oracle import fd_oracle as O
+
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(os.cpu_count())
+        threads = max((d.get("num_threads", 1) for d in threadpool_info()), default=1)
+    except Exception:  # threadpoolctl missing: BLAS picks its own count
+        threads = os.cpu_count()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    j = 0
+    while (len(times) < min_evals or time.perf_counter() < t_end) and (max_evals is None or len(times) < max_evals):
+        nw, wgu, wd = layers[j % len(layers)]
+        t0 = time.perf_counter()
+        x = O.post_attn_mlp(x, nw, wgu, wd, EPS, O.BF16)
+        times.append(time.perf_counter() - t0)
+        j += 1
+    return statistics.median(times) * 1e6, len(times), threads
+
+
+def run_reference(args) -> None:
+    """The reference arm: the reference's CPU formulation (oracle port) on host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    m = args.m
+    x, layers = cpu_layer_sample(2, m)
+    cpu_time_layers(x, layers, 0.0, max(1, args.warmup), max(1, args.warmup))  # warm-up
+    us, evals, threads = cpu_time_layers(x, layers, 0.0, args.steps, args.steps)
+    sample = f"{evals} single-layer steps over 2 seeded Llama-3-8B MLP layers, M={m}, numpy fp32 (oracle port of reference.py:66-79)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": us, "unit": "us/layer",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) weights rounded to bf16)",
+        "config": {"workload": f"post_attn_mlp Llama-3-8B widths M={m} (CPU, one layer per step)",
+                   "hidden": H, "intermediate": I, "m": m},
+        "cpu_baseline": {"value": us, "unit": "us/layer", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": us, "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU legs
+def make_layers(torch, device, layers, world=1, rank=0, dtype=None):
+    """Seeded layers (seed = layer index): norm_w = 1 + 0.1 N(0,1), weights N(0, 0.02).
+
+    With world > 1 each rank keeps only its tensor-parallel shard.
+    """
+    from fused_decode_b200 import tp
+
+    dtype = dtype or torch.bfloat16
+    out = []
+    for layer in range(layers):
+        g = torch.Generator(device=device)
+        g.manual_seed(layer)
+        nw = (1 + 0.1 * torch.randn(H, device=device, generator=g)).to(dtype)
+        wgu = torch.empty(2 * I, H, device=device, dtype=dtype)
+        wd = torch.empty(H, I, device=device, dtype=dtype)
+        # generate in chunks to bound the fp32 temporary
+        for r0 in range(0, 2 * I, 4096):
+            wgu[r0:r0 + 4096] = (torch.randn(min(4096, 2 * I - r0), H, device=device, generator=g) * 0.02).to(dtype)
+        for r0 in range(0, H, 1024):
+            wd[r0:r0 + 1024] = (torch.randn(min(1024, H - r0), I, device=device, generator=g) * 0.02).to(dtype)
+        if world > 1:
+            wgu, wd = tp.shard_gate_up(wgu, rank, world), tp.shard_down(wd, rank, world)
+        out.append((nw, wgu, wd))
+    return out
+
+
+def cuda_time(torch, fn, iters: int) -> float:
+    """Average ms per call of fn() over iters, CUDA events on the current stream."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def copy_roof_gbs(torch, device) -> float:
+    from fused_decode_b200 import kernels as K
+
+    n = 1 << 29  # 1 GiB of bf16 per buffer
+    a = torch.empty(n, device=device, dtype=torch.bfloat16).normal_()
+    b = torch.empty_like(a)
+    for _ in range(3):
+        K.launch_copy(b, a)
+    ms = cuda_time(torch, lambda: K.launch_copy(b, a), 10)
+    del a, b
+    return 2 * n * 2 / (ms * 1e-3) / 1e9
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from fused_decode_b200 import _capi, post_attn_mlp, tp
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200.stack import MlpStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    _capi.load()
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    pk = peaks()
+    layers = make_layers(torch, device, LAYERS, world, rank)
+
+    def layer_fn_tp(x, nw, wgu, wd):
+        return tp.TPPostAttnMlp(nw, wgu, wd, EPS)(x)
+
+    def build_stack(m):
+        fn = layer_fn_tp if world > 1 else None
+        return MlpStack(layers, m, EPS, kind="dot", layer_fn=fn)
+
+    def time_stack(stack, steps, warmup, sampler=None):
+        x0 = torch.randn(stack.static_in.shape, device=device, dtype=torch.bfloat16,
+                         generator=torch.Generator(device=device).manual_seed(1234))
+        stack.static_in.copy_(x0)
+        for _ in range(warmup):
+            stack.replay()
+        torch.cuda.synchronize()
+        barrier()
+        if sampler:
+            sampler.start()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        s.record()
+        for _ in range(steps):
+            stack.replay()
+        e.record()
+        torch.cuda.synchronize()
+        if sampler:
+            sampler.mark(t0, time.perf_counter())
+        clocks = sampler.stop() if sampler else None
+        barrier()
+        return max_over_ranks(s.elapsed_time(e) / steps), clocks
+
+    # ---- headline: M=1 stack
+    roof = copy_roof_gbs(torch, device) if rank == 0 else None
+    stack1 = build_stack(args.m)
+    sampler = ClockSampler(local) if rank == 0 else None
+    ms1, clocks = time_stack(stack1, args.steps, args.warmup, sampler)
+    us1 = ms1 * 1e3 / LAYERS
+    bytes1 = layer_bytes(args.m, world=world)
+    # ---- M=8 beside it
+    stack8 = build_stack(8)
+    ms8, _ = time_stack(stack8, args.steps, args.warmup)
+    us8 = ms8 * 1e3 / LAYERS
+    bytes8 = layer_bytes(8, world=world)
+
+    # ---- dominant kernel alone: the gate/up kernel, 32 launches per graph
+    mid = torch.empty(args.m, I // world, device=device, dtype=torch.bfloat16)
+    xk = torch.randn(args.m, H, device=device, dtype=torch.bfloat16)
+
+    def gate_up_all():
+        for nw, wgu, _ in layers:
+            K.mlp_gate_up_out(xk, nw, wgu, mid, EPS, "dot")
+
+    gate_up_all()
+    g_stream = torch.cuda.Stream()
+    g_stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(g_stream):
+        gate_up_all()
+    torch.cuda.current_stream().wait_stream(g_stream)
+    graph_gu = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_gu, stream=g_stream):
+        gate_up_all()
+    for _ in range(args.warmup):
+        graph_gu.replay()
+    ms_gu = max_over_ranks(cuda_time(torch, graph_gu.replay, args.steps)) / LAYERS
+    gu_bytes = gate_up_launch_bytes(args.m, world)
+    gu_gbs = gu_bytes / (ms_gu * 1e-3) / 1e9
+
+    # ---- e2e: public API with host buffers, every step H2D + 32 layers + D2H
+    host_in = torch.randn(args.m, H, dtype=torch.bfloat16).pin_memory()
+    host_out = torch.empty(args.m, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_graph_step():
+        out = stack1(host_in)  # H2D copy into the graph's input, replay
+        host_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    def e2e_eager_step():
+        x = host_in.to(device, non_blocking=True)
+        for nw, wgu, wd in layers:
+            x = layer_fn_tp(x, nw, wgu, wd) if world > 1 else post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot")
+        host_out.copy_(x, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    def wall(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        dt = (time.perf_counter() - t0) / steps
+        barrier()
+        return max_over_ranks(dt)
+
+    e2e_s = wall(e2e_graph_step, args.steps)
+    e2e_eager_s = wall(e2e_eager_step, max(3, args.steps // 10))
+
+    # ---- CPU baseline (rank 0, N=1 only): oracle port, bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        xs, cl = cpu_layer_sample(2, args.m)
+        cpu_time_layers(xs, cl, 0.0, 1, 1)
+        us_cpu, evals, threads = cpu_time_layers(xs, cl, args.cpu_seconds, 3)
+        cpu = {"value": us_cpu, "unit": "us/layer", "cores": threads, "kind": "port",
+               "sample": f"{evals} layer evaluations over 2 seeded Llama-3-8B MLP layers at M={args.m} "
+                         f"(numpy fp32 oracle port of reference.py:66-79), ~{args.cpu_seconds:.0f} s"}
+
+    if rank == 0:
+        traffic = committed_traffic().get("gate_up_kernel_bytes_per_launch")
+        gbs1 = bytes1 / (us1 * 1e-6) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": us1,
+            "unit": "us/layer",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms1,
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": us1 / PUBLISHED_US[1] if args.m == 1 else None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded random-init Llama-3-8B MLP weights, N(0,0.02))",
+            "config": {
+                "workload": f"post_attn_mlp Llama-3-8B widths, M={args.m}, {LAYERS} layers in one CUDA graph"
+                            + (f", tensor-parallel x{world} (NCCL allreduce per layer)" if world > 1 else ""),
+                "hidden": H, "intermediate": I, "m": args.m, "layers": LAYERS, "kind": "dot",
+                "parallelism": f"tp{world}" if world > 1 else "single",
+                "l2": f"inputs larger than L2: {LAYERS * layer_bytes(args.m, world=world) / 1e9:.1f} GB of weights per step per GPU",
+            },
+            "hbm_gbs": gbs1,
+            "hbm_frac": gbs1 / pk["hbm_gbs"],
+            "copy_roof_gbs": roof,
+            "m8": {"us_per_layer": us8, "ms_per_step": ms8, "hbm_gbs": bytes8 / (us8 * 1e-6) / 1e9,
+                   "hbm_frac": bytes8 / (us8 * 1e-6) / 1e9 / pk["hbm_gbs"]},
+            "roofline": {
+                "kernel": "gemv_streamk_kernel gate/up mode (RMSNorm + gate/up GEMV + SwiGLU)",
+                "bound": "hbm", "achieved": gu_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": gu_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
+                "traffic": traffic, "bytes_per_launch": gu_bytes, "us_per_launch": ms_gu * 1e3,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_s * 1e6 / LAYERS, "unit": "us/layer",
+                    "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+                    "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
+                    "api": "fused_decode_b200.stack.MlpStack (pinned host in, graph replay, pinned host out)",
+                    "eager_api_us_per_layer": e2e_eager_s * 1e6 / LAYERS},
+            # per layer: gate/up kernel + down kernel (+ residual-add kernel under TP)
+            "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 3),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del stack1, stack8, graph_gu
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

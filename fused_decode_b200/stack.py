@@ -1,0 +1,82 @@
+"""A stack of post-attention MLP layers replayed as one CUDA graph.
+
+The reference times ``post_attn_mlp`` inside a CUDA graph (bench.py:451-472)
+to take host launch cost out of the step.  ``MlpStack`` is that as a reusable
+object: it captures ``layers`` consecutive ``post_attn_mlp`` calls (two
+kernels each) on a private stream, and ``__call__`` copies the input into the
+graph's static buffer, replays, and returns the static output.  With
+``tp_group`` set it captures the tensor-parallel layer instead
+(``fused_decode_b200.tp``).
+"""
+
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from fused_decode_b200 import kernels as K
+from fused_decode_b200.ops import _check_activation, post_attn_mlp
+
+
+class MlpStack:
+    """``layers`` of ``(norm_weight, w_gate_up, w_down)`` applied in order.
+
+    ``batch`` rows of width H are fixed at construction (a CUDA graph has
+    static shapes).  Replays are stream-ordered on the caller's current
+    stream.
+    """
+
+    def __init__(
+        self,
+        layers: Sequence[tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
+        batch: int,
+        eps: float = 1e-6,
+        *,
+        kind: str | None = None,
+        layer_fn=None,
+    ) -> None:
+        if not layers:
+            raise ValueError("need at least one layer")
+        nw0, wgu0, wd0 = layers[0]
+        _check_activation(wgu0, "w_gate_up")
+        self.layers = list(layers)
+        self.eps = float(eps)
+        self.kind = K.resolve_kind(kind)
+        self.h = int(wgu0.shape[1])
+        self.device = wgu0.device
+        self.dtype = wgu0.dtype
+        self._fn = layer_fn or (lambda x, nw, wgu, wd: post_attn_mlp(x, nw, wgu, wd, self.eps, kind=self.kind))
+        self.static_in = torch.zeros(batch, self.h, device=self.device, dtype=self.dtype)
+        self._stream = torch.cuda.Stream(device=self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        self._capture()
+
+    def _run(self, x: torch.Tensor) -> torch.Tensor:
+        for nw, wgu, wd in self.layers:
+            x = self._fn(x, nw, wgu, wd)
+        return x
+
+    def _capture(self) -> None:
+        cur = torch.cuda.current_stream(self.device)
+        self._stream.wait_stream(cur)
+        with torch.cuda.stream(self._stream):
+            self._run(self.static_in)  # first call sizes the workspace outside capture
+        cur.wait_stream(self._stream)
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(self.graph, stream=self._stream):
+            self.static_out = self._run(self.static_in)
+
+    @property
+    def launches_per_replay(self) -> int:
+        return 2 * len(self.layers)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.static_out
+
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Copy ``hidden`` (device or pinned host) in, replay, return the output."""
+        self.static_in.copy_(hidden, non_blocking=True)
+        self.graph.replay()
+        return self.static_out

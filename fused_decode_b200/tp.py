@@ -1,0 +1,89 @@
+"""Tensor-parallel post-attention MLP (Megatron split) over NCCL.
+
+Each of T ranks holds the gate rows ``[r*I/T, (r+1)*I/T)`` of ``w_gate_up``
+together with the matching up rows ``I + [r*I/T, (r+1)*I/T)``, restacked as its
+own ``[2I/T, H]`` weight, and the column slice ``w_down[:, r*I/T:(r+1)*I/T]``.
+A layer is: the fused MLP kernels on the local shard with an fp32 partial and
+no residual, one ``all_reduce(sum)`` of the ``[M, H]`` fp32 partials over
+NVLink, then ``out = round(sum + hidden)``.  RMSNorm is recomputed on every rank
+(hidden is replicated), so the allreduce is the only exchange.
+
+The reference has no multi-GPU path; this is the tensor-parallel layout of
+its ``post_attn_mlp`` (ops.py:283-315) that the B200 build adds.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from fused_decode_b200 import kernels as K
+
+
+def shard_bounds(inner: int, rank: int, world: int) -> tuple[int, int]:
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world {world}")
+    if inner % world:
+        raise ValueError(f"intermediate size {inner} is not divisible by {world} ranks")
+    per = inner // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_gate_up(w_gate_up: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's ``[2I/T, H]`` restack: its gate rows, then the matching up rows."""
+    two_i = w_gate_up.shape[0]
+    if two_i % 2:
+        raise ValueError("w_gate_up must have an even number of rows [2I, H]")
+    inner = two_i // 2
+    lo, hi = shard_bounds(inner, rank, world)
+    return torch.cat((w_gate_up[lo:hi], w_gate_up[inner + lo:inner + hi]), dim=0).contiguous()
+
+
+def shard_down(w_down: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's ``[H, I/T]`` column slice of ``w_down`` (made contiguous)."""
+    lo, hi = shard_bounds(w_down.shape[1], rank, world)
+    return w_down[:, lo:hi].contiguous()
+
+
+class TPPostAttnMlp:
+    """One tensor-parallel MLP layer on this rank.
+
+    ``__call__(hidden)`` returns ``post_attn_mlp(hidden, ...)`` of the full
+    (unsharded) weights on every rank.  All ranks must call it in the same
+    order with the same ``hidden``.
+    """
+
+    def __init__(self, norm_weight, w_gate_up_shard, w_down_shard, eps=1e-6, *, kind=None,
+                 group=None) -> None:
+        self.norm_weight = norm_weight
+        self.w_gate_up = w_gate_up_shard
+        self.w_down = w_down_shard
+        self.eps = float(eps)
+        self.kind = K.resolve_kind(kind)
+        self.group = group
+        if self.w_gate_up.shape[0] != 2 * self.w_down.shape[1]:
+            raise ValueError("gate/up shard rows must be twice the down shard columns")
+        if self.w_gate_up.shape[1] != self.w_down.shape[0]:
+            raise ValueError("gate/up shard and down shard disagree on H")
+
+    @classmethod
+    def from_full(cls, norm_weight, w_gate_up, w_down, rank, world, eps=1e-6, *, kind=None, group=None):
+        return cls(norm_weight, shard_gate_up(w_gate_up, rank, world), shard_down(w_down, rank, world),
+                   eps, kind=kind, group=group)
+
+    def partial(self, hidden2: torch.Tensor) -> torch.Tensor:
+        """This rank's fp32 ``[M, H]`` down-projection partial (no residual)."""
+        m, h = hidden2.shape
+        part = torch.empty(m, h, device=hidden2.device, dtype=torch.float32)
+        K.post_attn_mlp_out(hidden2, self.norm_weight, self.w_gate_up, self.w_down, part, self.eps,
+                            self.kind, add_residual=False)
+        return part
+
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        h = hidden.shape[-1]
+        hidden2 = hidden.reshape(-1, h).contiguous()
+        part = self.partial(hidden2)
+        dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+        out = torch.empty(hidden.shape, device=hidden.device, dtype=hidden.dtype)
+        K.residual_add_out(part, hidden2, out.view(-1, h))
+        return out

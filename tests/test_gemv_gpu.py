@@ -1,0 +1,205 @@
+"""GEMV family and fused MLP at the BASELINE shapes, plus edge cases.
+
+Comparator: the CPU oracle (fp32 numpy restatement of reference.py:50-79).
+Tolerance: BASELINE's atol = rtol = 1e-2 for fp16/bf16 outputs against the
+fp32 reference.  Split-K partial sums are reduced in a fixed order, so the
+CUDA results are also checked to be bit-reproducible run to run.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fd_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+from fused_decode_b200 import linear_decode, post_attn_mlp  # noqa: E402
+from fused_decode_b200 import kernels as K  # noqa: E402
+
+TOL = {"rtol": 1e-2, "atol": 1e-2}
+_NAME = {torch.float16: "float16", torch.bfloat16: "bfloat16"}
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _close(actual, expected_np, tol=TOL):
+    expected = torch.from_numpy(np.ascontiguousarray(expected_np)).to(actual.device)
+    assert actual.shape == expected.shape, (actual.shape, expected.shape)
+    torch.testing.assert_close(actual.float(), expected, **tol)
+
+
+def _gen(seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    return g
+
+
+# M in {1,2,4,8,16} x (N,K) in the Llama-3-8B shapes.
+SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (28672, 4096)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,k", SHAPES)
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 16])
+def test_linear_baseline_shapes(dtype, n, k, m):
+    g = _gen(1000 + m)
+    x = torch.randn(m, k, device="cuda", dtype=dtype, generator=g)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(dtype)
+    bias = (torch.randn(n, device="cuda", generator=g) * 0.02).to(dtype)
+    row = torch.randn(m, n, device="cuda", dtype=dtype, generator=g)
+    ref = O.linear(_np(x), _np(w), _np(bias), _np(row), _NAME[dtype])
+    kinds = ["dot", "simt"] if (n, k) in [(4096, 4096), (4096, 14336)] or m in (1, 16) else ["dot"]
+    for kind in kinds:
+        y = linear_decode(x, w, bias, row_add=row, kind=kind)
+        _close(y, ref)
+
+
+@pytest.mark.parametrize("kind", ["dot", "simt"])
+@pytest.mark.parametrize("m", list(range(1, 17)))
+def test_linear_every_m(kind, m):
+    """Every batch size 1..16 on a shape whose N and K are not tile multiples."""
+    g = _gen(m)
+    n, k = 200, 72  # 200 rows = 1 full + 1 partial block; K = 2 steps + 8 columns
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    bias = torch.randn(n, device="cuda", dtype=torch.float32, generator=g)
+    y = linear_decode(x, w, bias, kind=kind)
+    _close(y, O.linear(_np(x), _np(w), _np(bias), None, "bfloat16"))
+
+
+def test_linear_layouts_and_broadcasts():
+    g = _gen(7)
+    dt = torch.float16
+    m, n, k = 5, 384, 512
+    x = torch.randn(m, k, device="cuda", dtype=dt, generator=g) * 0.1
+    w = torch.randn(n, k, device="cuda", dtype=dt, generator=g) * 0.1
+    ref = O.linear(_np(x), _np(w), None, None, "float16")
+    # 1-D input -> [N]
+    y1 = linear_decode(x[0], w)
+    assert y1.shape == (n,)
+    _close(y1, ref[0])
+    # 3-D input keeps leading dims
+    y3 = linear_decode(x.view(5, 1, k), w)
+    assert y3.shape == (5, 1, n)
+    _close(y3, ref.reshape(5, 1, n))
+    # row_add broadcasts: [N], [1,N], [M,1], fp32
+    ra_n = torch.randn(n, device="cuda", dtype=torch.float32, generator=g)
+    _close(linear_decode(x, w, row_add=ra_n), O.linear(_np(x), _np(w), None, np.broadcast_to(_np(ra_n), (m, n)), "float16"))
+    ra_m1 = torch.randn(m, 1, device="cuda", dtype=dt, generator=g)
+    _close(linear_decode(x, w, row_add=ra_m1), O.linear(_np(x), _np(w), None, np.broadcast_to(_np(ra_m1), (m, n)), "float16"))
+    # out= provided
+    out = torch.empty(m, n, device="cuda", dtype=dt)
+    r = linear_decode(x, w, out=out)
+    assert r.data_ptr() == out.data_ptr()
+    _close(out, ref)
+    # strided x rows (row stride 2K) and a misaligned x (generic path)
+    xs = torch.randn(m, 2 * k, device="cuda", dtype=dt, generator=g)[:, :k]
+    _close(linear_decode(xs, w), O.linear(_np(xs), _np(w), None, None, "float16"))
+    buf = torch.randn(m * k + 1, device="cuda", dtype=dt, generator=g)
+    xm = buf[1:].view(m, k)
+    assert xm.data_ptr() % 16 != 0
+    _close(linear_decode(xm, w), O.linear(_np(xm), _np(w), None, None, "float16"))
+    # empty batch
+    assert linear_decode(x[:0], w).shape == (0, n)
+
+
+@pytest.mark.parametrize("kind", ["dot", "simt"])
+def test_linear_deterministic(kind):
+    g = _gen(3)
+    x = torch.randn(8, 14336, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.randn(4096, 14336, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    y0 = linear_decode(x, w, kind=kind)
+    for _ in range(3):
+        assert torch.equal(linear_decode(x, w, kind=kind), y0)
+
+
+def _mlp_weights(h, i, dtype, seed):
+    g = _gen(seed)
+    nw = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dtype)
+    wgu = (torch.randn(2 * i, h, device="cuda", generator=g) * 0.02).to(dtype)
+    wd = (torch.randn(h, i, device="cuda", generator=g) * 0.02).to(dtype)
+    return nw, wgu, wd
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m", [1, 3, 8, 16])
+def test_post_attn_mlp_llama8b(dtype, m):
+    """hidden [M, 4096], w_gate_up [28672, 4096], w_down [4096, 14336]."""
+    h, i = 4096, 14336
+    nw, wgu, wd = _mlp_weights(h, i, dtype, 11)
+    x = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(12 + m))
+    ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-5, _NAME[dtype])
+    for kind in ("dot", "simt"):
+        y = post_attn_mlp(x, nw, wgu, wd, 1e-5, kind=kind)
+        assert y.shape == x.shape and y.is_contiguous()
+        _close(y, ref)
+
+
+@pytest.mark.parametrize("h,i", [(64, 128), (128, 200), (192, 320), (520, 1000)])
+def test_post_attn_mlp_ragged(h, i):
+    """Widths that are not multiples of the block sizes (64 gate rows, 128 down rows)."""
+    dtype = torch.bfloat16
+    nw, wgu, wd = _mlp_weights(h, i, dtype, h + i)
+    for m in (1, 5, 16):
+        x = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(m))
+        ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-6, "bfloat16")
+        _close(post_attn_mlp(x, nw, wgu, wd), ref)
+
+
+def test_post_attn_mlp_no_residual_partial():
+    """The tensor-parallel partial (no residual) through the launcher."""
+    h, i, m = 256, 384, 4
+    nw, wgu, wd = _mlp_weights(h, i, torch.bfloat16, 5)
+    x = torch.randn(m, h, device="cuda", dtype=torch.bfloat16, generator=_gen(5))
+    out = torch.empty_like(x)
+    K.post_attn_mlp_out(x, nw, wgu, wd, out, 1e-6, "dot", add_residual=False)
+    ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-6, "bfloat16", add_residual=False)
+    _close(out, ref)
+
+
+def test_post_attn_mlp_graph_stack():
+    """Eight layers captured in one CUDA graph: replays reproduce the eager
+    result bit for bit (the split-K workspace resets itself between launches)."""
+    h, i, m, layers = 512, 1024, 8, 8
+    dtype = torch.bfloat16
+    ws = [_mlp_weights(h, i, dtype, 50 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(9))
+
+    def stack(x):
+        for nw, wgu, wd in ws:
+            x = post_attn_mlp(x, nw, wgu, wd, 1e-5)
+        return x
+
+    eager = stack(x0)
+    ref = _np(x0)
+    for nw, wgu, wd in ws:
+        ref = O.post_attn_mlp(ref, _np(nw), _np(wgu), _np(wd), 1e-5, "bfloat16")
+    _close(eager, ref, {"rtol": 2e-2, "atol": 2e-2})
+
+    static_in = x0.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        stack(static_in)  # warm the workspace on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = stack(static_in)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(static_out, eager)
+
+
+def test_mlp_fallback_layout():
+    """A w_down with a non-unit column stride takes the composed path."""
+    h, i, m = 128, 256, 3
+    nw, wgu, wd = _mlp_weights(h, i, torch.float16, 21)
+    wd_t = wd.t().contiguous().t()
+    assert wd_t.stride(1) != 1
+    x = torch.randn(m, h, device="cuda", dtype=torch.float16, generator=_gen(4))
+    ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-6, "float16")
+    _close(post_attn_mlp(x, nw, wgu, wd_t, kind="dot"), ref)
