@@ -58,6 +58,7 @@ SIGNATURES: dict[str, tuple] = {
     "fd_swiglu_out": (c_i32, [_P_ROWS, _P_ROWS, _P_ROWS, c_vp]),
     "fd_rope_out": (c_i32, [_P_ROWS, _P_ROWS, _P_ROWS, _P_ROWS, c_vp]),
     "fd_linear_workspace_bytes": (c_size, [c_i32, c_i64, c_i64]),
+    "fd_workspace_status_offset": (c_size, []),
     "fd_linear_out": (
         c_i32,
         [

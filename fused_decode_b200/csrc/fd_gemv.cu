@@ -1,55 +1,65 @@
 // Small-batch GEMV family (M = 1..16) and the fused post-attention MLP.
 //
-// Design (sm_100a, HBM-bound):
-//  * Stream-K over the weight.  The weight is cut into blocks of BR rows; each
-//    block is a run of KS "steps" of 32 columns.  The grid (a multiple of the
-//    SM count) splits the flat step range [0, nblocks*KS) into equal contiguous
-//    pieces, so every CTA streams the same number of weight bytes whatever N
-//    and K are (the reference grid is cdiv(N, 64) CTAs with no split-K,
-//    kernels.py:775, which leaves most SMs idle at N=4096).
-//  * Each warp owns 16 rows of the block.  Per step a lane issues two 16-byte
-//    loads (rows g and g+8, columns 8q..8q+7 of the step, g = lane/4,
-//    q = lane%4) and keeps D steps in flight in a register ring.
-//  * "dot" kind: the 16 x 32 tile feeds two mma.sync m16n8k16 (swap-AB: the
-//    weight is the A operand, the batch is N=8 or 16).  The 32 physical columns
-//    a lane holds are assigned to logical MMA k-indices by a fixed permutation
-//    that is applied identically to A and B, so the sum is unchanged and the
-//    loads stay 16 bytes wide.
-//  * "simt" kind: the same loads, fp32 FMAs against all M rows of x, then a
-//    4-lane shuffle reduction.
-//  * Split-K partials go to per-CTA slots in a workspace; the last CTA to
-//    finish a block (an atomic counter) sums the slots in CTA order --
-//    deterministic, no spin-wait -- applies the epilogue and re-zeroes the
-//    counter so the workspace is ready for the next launch / graph replay.
-//  * The fused MLP's gate/up kernel computes RMSNorm of the (tiny) hidden
-//    batch into shared memory in its prologue, pairs 64 gate rows with the
-//    matching 64 up rows in each block, and applies SwiGLU in the epilogue;
-//    the down kernel adds the residual in its epilogue.  Both launch with
-//    programmatic dependent launch: the weight prefetch of the next kernel
-//    is issued before griddepcontrol.wait.
+// Design (sm_100a, HBM-bound: a weight byte is used 2*M times):
+//  * Stream-K over the weight.  The weight is cut into blocks of 128 rows; a
+//    block is a run of KS steps of 64 columns.  The grid (one CTA per SM)
+//    splits the flat step range [0, nblocks*KS) into equal contiguous pieces,
+//    so every SM streams the same number of weight bytes whatever N and K are.
+//    (The reference launches cdiv(N, 64) CTAs with no split-K, kernels.py:775,
+//    which leaves most of 148 SMs idle at N = 4096.)
+//  * TMA pipeline.  A producer warp issues 2-D tensor-map loads
+//    (cp.async.bulk.tensor, 128-byte swizzle) of each step's [128 x 64] weight
+//    tile -- and, for a plain GEMV, the [M x 64] activation tile -- into an
+//    S-stage shared-memory ring guarded by mbarriers.  Out-of-range rows and
+//    columns are zero-filled by the TMA unit, so ragged N and K need no masks.
+//  * Eight consumer warps own 16 weight rows each.  "dot" kind: each lane
+//    reads 16 contiguous columns of its two rows (rows g and g+8, g = lane/4,
+//    q = lane%4) -- conflict-free under the 128B swizzle -- and feeds four
+//    mma.sync m16n8k16 per step (swap-AB: weight = A, batch = N of 8 or 16).
+//    The physical columns a lane holds are assigned to logical MMA k-indices
+//    by one fixed permutation applied to both A and B, so the sum is exact.
+//    "simt" kind: the same tiles, fp32 FMAs against all M rows.
+//  * Split-K partials go to per-CTA slots in a caller workspace; the last CTA
+//    to finish a block (an atomic counter) sums the slots in CTA order --
+//    deterministic, no inter-CTA waiting -- applies the epilogue and re-zeroes
+//    the counter, so the workspace is ready for the next launch or replay.
+//  * Every mbarrier wait is bounded (globaltimer, 2 s): on expiry the CTA sets
+//    a bit in the workspace status word and leaves instead of hanging.
+//  * The MLP gate/up kernel computes RMSNorm of the (tiny) hidden batch into
+//    shared memory in its prologue, pairs 64 gate rows with the matching 64 up
+//    rows in each block and applies SwiGLU in the epilogue; the down kernel
+//    adds the residual in its epilogue.  Kernels launch with programmatic
+//    dependent launch: the weight prefetch is issued before griddepcontrol.wait.
 #include "fd_common.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <cstdlib>
 
 using namespace fd;
 
 namespace {
 
-constexpr int GW = 8;           // warps per CTA
-constexpr int BR = GW * 16;     // weight rows per block
-constexpr int KSTEP = 32;       // columns per step
-constexpr int MT_MAX = 16;      // max batch rows
-constexpr int XPAD = 64;        // bytes of padding per shared x row: pitch = 64 mod 128 B,
-                                // so the 8 lanes of a 16-byte load phase hit distinct banks
+constexpr int GW = 8;             // consumer warps per CTA
+constexpr int BR = GW * 16;       // weight rows per block
+constexpr int KC = 64;            // columns per step (128 bytes of a 16-bit row)
+constexpr int MT_MAX = 16;        // max batch rows
+constexpr int CONSUMERS = GW * 32;
+constexpr int THREADS = CONSUMERS + 32;  // + one producer warp
+constexpr int W_STAGE_BYTES = BR * KC * 2;  // 16 KB
+constexpr int MAX_STAGES = 8;
+constexpr int64_t kMaxCounters = 1 << 16;   // blocks per launch (N <= 8M rows)
+constexpr uint64_t kWaitNs = 2000000000ull; // bounded mbarrier waits: 2 s
+
+// Status bits written to the workspace status word.
+constexpr int kStatusFullTimeout = 1;
+constexpr int kStatusEmptyTimeout = 2;
 
 enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1 };
 
 struct GemvArgs {
-  // operands (all strides in elements; k-stride of x and w is 1)
-  const char* x;
-  int64_t sxm;
-  const char* w;
-  int64_t swn;
   const void* bias;
   int32_t bias_dtype;
   int64_t sbias;
@@ -65,16 +75,17 @@ struct GemvArgs {
   int64_t ks;       // steps per block
   int64_t nblocks;
   int64_t total;    // nblocks * ks
+  int32_t stages;
   float* slots;     // [grid][2][BR * MT_MAX]
   int* counters;    // [nblocks]
+  int* status;      // error bits
   // gate/up mode
   int64_t inner;            // I: up rows start at row I of w
-  const void* hidden;       // [m, k] contiguous rows (row stride hidden_stride)
+  const void* hidden;       // [m, k] rows, row stride hidden_stride
   int64_t hidden_stride;
   const void* norm_w;
   int32_t norm_dtype;
   float eps;
-  int32_t xs_pitch;         // shared x row pitch in elements
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -100,25 +111,74 @@ FD_DEV void mma16816<__half>(float* c, uint32_t a0, uint32_t a1, uint32_t a2, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Weight stream: read once, do not keep in L1, evict early from L2.
-FD_DEV uint4 ld_weight16(const void* p, uint64_t policy) {
-  uint4 v;
+FD_DEV uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+FD_DEV uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+FD_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+FD_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+FD_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+FD_DEV uint32_t mbar_try(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
   asm volatile(
-      "ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "l"(p), "l"(policy));
-  return v;
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.b32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok;
+}
+// Wait for the phase with the given parity to complete; false after kWaitNs.
+FD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  if (mbar_try(addr, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try(addr, parity)) return true;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
 }
 FD_DEV uint64_t evict_first_policy() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-FD_DEV uint4 lds16(const void* p) {
-  return *reinterpret_cast<const uint4*>(p);
+// 2-D tiled TMA load into this CTA's shared memory, completing on `bar`.
+FD_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar,
+                        uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
 }
+FD_DEV void tma_load_2d_plain(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+FD_DEV void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+FD_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS) : "memory"); }
 FD_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 FD_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk c of row r inside a 128B-swizzled tile whose
+// rows are 128 bytes (TMA CU_TENSOR_MAP_SWIZZLE_128B, 1024-byte aligned base).
+FD_DEV uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // ------------------------------------------------------------ stream-K split
 FD_DEV int64_t range_start(int64_t c, int64_t total, int64_t G) { return c * total / G; }
@@ -126,6 +186,7 @@ FD_DEV int64_t range_start(int64_t c, int64_t total, int64_t G) { return c * tot
 FD_DEV int64_t cta_of(int64_t t, int64_t total, int64_t G) { return ((t + 1) * G - 1) / total; }
 
 FD_DEV float silu_mul(float g, float u) {
+  // Stable sigmoid, as the reference kernel computes it (kernels.py:448-451).
   const float e = expf(-fabsf(g));
   const float sig = g >= 0.f ? 1.0f / (1.0f + e) : e / (1.0f + e);
   return g * sig * u;
@@ -137,13 +198,19 @@ FD_DEV float silu_mul(float g, float u) {
 template <int NT>
 struct Acc {
   float v[NT][4];
+  FD_DEV void zero() {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[t][e] = 0.f;
+  }
 };
 
 // ------------------------------------------------------------ epilogues
 template <typename T, int NT, int MODE>
 struct Epilogue;
 
-// Plain linear: y = round(acc + bias + row_add).
+// Plain linear: y = round(acc + bias + row_add)  (or the fp32 sum).
 template <typename T, int NT>
 struct Epilogue<T, NT, MODE_LINEAR> {
   FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* /*xchg*/) {
@@ -188,7 +255,7 @@ struct Epilogue<T, NT, MODE_GATEUP> {
           xchg[r * MT_MAX + col] = acc.v[t][e];
         }
     }
-    __syncthreads();
+    consumer_sync();
     if (warp < HALF) {
 #pragma unroll
       for (int t = 0; t < NT; ++t)
@@ -204,101 +271,178 @@ struct Epilogue<T, NT, MODE_GATEUP> {
           }
         }
     }
-    __syncthreads();
+    consumer_sync();
   }
 };
 
-// ------------------------------------------------------------ the kernel
-// KIND 0 = dot (mma.sync), 1 = simt.  MP = padded batch for simt (1..16).
-// XS = x lives in shared memory (gate/up mode with the norm fused).
-template <typename T, int NT, int KIND, int MP, int MODE, bool XS, int D>
-__global__ void __launch_bounds__(GW * 32, 2) gemv_streamk_kernel(const GemvArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_last;
+// Block `blk` ends inside this CTA's range [s0, s1): finish it directly if the
+// CTA covered all of it, else publish the partial and let the last of the
+// block's CTAs reduce.  Called by all consumer threads together.
+template <typename T, int NT, int MODE>
+FD_DEV void flush_block(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* xchg, int64_t s0,
+                        int64_t s1, int64_t G, int64_t c, int* s_last) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
+  const bool covered = (s0 <= blk * a.ks) && (s1 >= (blk + 1) * a.ks);
+  if (covered) {
+    Epilogue<T, NT, MODE>::run(a, blk, acc, xchg);
+    return;
+  }
+  const int slot = (blk == s0 / a.ks) ? 0 : 1;
+  float* sp = a.slots + (c * 2 + slot) * (BR * MT_MAX);
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 16 * warp + g + 8 * h;
+      const int col = 8 * t + 2 * q;
+      *reinterpret_cast<float2*>(sp + r * MT_MAX + col) = make_float2(acc.v[t][2 * h], acc.v[t][2 * h + 1]);
+    }
+  __threadfence();
+  consumer_sync();
+  const int64_t cf = cta_of(blk * a.ks, a.total, G);
+  const int64_t cl = cta_of((blk + 1) * a.ks - 1, a.total, G);
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(a.counters + blk, 1);
+    *s_last = (old == static_cast<int>(cl - cf));
+  }
+  consumer_sync();
+  if (*s_last) {
+    __threadfence();
+    Acc<NT> sum;
+    sum.zero();
+    for (int64_t cc = cf; cc <= cl; ++cc) {
+      const int sl = (blk == range_start(cc, a.total, G) / a.ks) ? 0 : 1;
+      const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = 16 * warp + g + 8 * h;
+          const int col = 8 * t + 2 * q;
+          const float2 v = __ldcg(reinterpret_cast<const float2*>(rp + r * MT_MAX + col));
+          sum.v[t][2 * h] += v.x;
+          sum.v[t][2 * h + 1] += v.y;
+        }
+    }
+    Epilogue<T, NT, MODE>::run(a, blk, sum, xchg);
+    if (threadIdx.x == 0) a.counters[blk] = 0;
+  }
+}
+
+// ------------------------------------------------------------ the TMA kernel
+// KIND 0 = dot (mma.sync), 1 = simt.  MP = padded batch for simt (1..16).
+// NT * 8 = batch rows of the activation tile (8 or 16).
+template <typename T, int NT, int KIND, int MP, int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
+                    const __grid_constant__ CUtensorMap xmap, const GemvArgs a) {
+  constexpr int MT = NT * 8;
+  constexpr int X_STAGE_BYTES = MT * KC * 2;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ int s_last;
+  __shared__ int s_abort;
+  // 1024-byte alignment for the 128B swizzle atoms.
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~static_cast<uintptr_t>(1023));
+  const int S = a.stages;
+  unsigned char* wst = smem;                                          // S x 16 KB
+  unsigned char* xst = wst + static_cast<size_t>(S) * W_STAGE_BYTES;  // LINEAR: S x MT x 128 B
+  // GATEUP: normed x, ceil(k/64) chunks of [m rows x 128 B], swizzled like a TMA tile
+  unsigned char* xs = xst;
+  const int64_t xs_bytes = MODE == MODE_GATEUP ? a.ks * a.m * 128 : static_cast<int64_t>(S) * X_STAGE_BYTES;
+  float* xchg = reinterpret_cast<float*>(xst + ((xs_bytes + 15) & ~15ll));
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(xchg) + (BR / 2) * MT_MAX * 4);
+  uint64_t* empty = full + MAX_STAGES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t G = gridDim.x, c = blockIdx.x;
   const int64_t s0 = range_start(c, a.total, G);
   const int64_t s1 = range_start(c + 1, a.total, G);
-  const uint64_t pol = evict_first_policy();
 
-  T* xs = reinterpret_cast<T*>(smem);  // [m][xs_pitch] when XS
-  float* xchg = reinterpret_cast<float*>(smem + (XS ? static_cast<size_t>(a.m) * a.xs_pitch * sizeof(T) : 0));
-
-  // Weight row of this lane for block `blk` and half `hh` (row g or g+8).
-  auto wrow = [&](int64_t blk, int hh, bool& ok) -> const T* {
-    int64_t r;
-    if (MODE == MODE_GATEUP) {
-      const int w4 = warp & (GW / 2 - 1);
-      const int64_t j = blk * (BR / 2) + 16 * w4 + g + 8 * hh;
-      ok = j < a.inner;
-      r = (warp >= GW / 2) ? a.inner + j : j;
-    } else {
-      r = blk * BR + 16 * warp + g + 8 * hh;
-      ok = r < a.n;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], GW);
     }
-    return reinterpret_cast<const T*>(a.w) + (ok ? r : 0) * a.swn;
-  };
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
 
-  // -------- register ring
-  uint4 ra_[D], rb_[D], rx_[D][NT];
-  // load cursor
-  int64_t lt = s0, lb = s0 / a.ks, lk = s0 - (s0 / a.ks) * a.ks;
-  bool ok0, ok1;
-  const T* wr0 = wrow(lb, 0, ok0);
-  const T* wr1 = wrow(lb, 1, ok1);
-
-  auto load_w = [&](int i) {
-    const int64_t col = lk * KSTEP + 8 * q;
-    const bool kin = col < a.k;
-    ra_[i] = (ok0 && kin) ? ld_weight16(wr0 + col, pol) : make_uint4(0, 0, 0, 0);
-    rb_[i] = (ok1 && kin) ? ld_weight16(wr1 + col, pol) : make_uint4(0, 0, 0, 0);
-  };
-  auto load_x = [&](int i, int64_t kk) {
-    if (KIND == 0) {
-      const int64_t col = kk * KSTEP + 8 * q;
-      const bool kin = col < a.k;
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const int mrow = g + 8 * t;
-        if (kin && mrow < a.m) {
-          if (XS)
-            rx_[i][t] = lds16(xs + mrow * a.xs_pitch + col);
-          else
-            rx_[i][t] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.x) + mrow * a.sxm + col));
+  if (warp == GW) {
+    // ================= producer warp (one lane issues every copy)
+    if (lane == 0) {
+      prefetch_map(&wmap);
+      if (MODE == MODE_GATEUP) prefetch_map(&umap);
+      else prefetch_map(&xmap);
+      const uint64_t pol = evict_first_policy();
+      const uint32_t stage_bytes = W_STAGE_BYTES + (MODE == MODE_LINEAR ? X_STAGE_BYTES : 0);
+      const int64_t b0 = s0 / a.ks, k0 = s0 - (s0 / a.ks) * a.ks;
+      const int64_t n_steps = s1 - s0;
+      const int64_t npre = n_steps < S ? n_steps : S;
+      // (1) weight tiles of the first stages: independent of the previous kernel
+      int64_t pb = b0, pk = k0;
+      for (int64_t it = 0; it < npre; ++it) {
+        mbar_expect_tx(&full[it], stage_bytes);
+        unsigned char* dst = wst + it * W_STAGE_BYTES;
+        if (MODE == MODE_GATEUP) {
+          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * (BR / 2)), &full[it], pol);
+          tma_load_2d(dst + W_STAGE_BYTES / 2, &umap, static_cast<int32_t>(pk * KC),
+                      static_cast<int32_t>(pb * (BR / 2)), &full[it], pol);
         } else {
-          rx_[i][t] = make_uint4(0, 0, 0, 0);
+          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * BR), &full[it], pol);
+        }
+        if (++pk == a.ks) { pk = 0; ++pb; }
+      }
+      // (2) activation tiles read the previous kernel's output
+      if (MODE == MODE_LINEAR) {
+        grid_dep_wait();
+        int64_t xb = b0, xk = k0;
+        for (int64_t it = 0; it < npre; ++it) {
+          tma_load_2d_plain(xst + it * X_STAGE_BYTES, &xmap, static_cast<int32_t>(xk * KC), 0, &full[it]);
+          if (++xk == a.ks) { xk = 0; ++xb; }
         }
       }
+      // (3) steady state: refill a stage once all consumer warps released it
+      int64_t issued = npre;
+      for (int64_t it = npre; it < n_steps; ++it) {
+        const int s = static_cast<int>(it % S);
+        if (!mbar_wait(&empty[s], static_cast<uint32_t>((it / S - 1) & 1))) {
+          atomicOr(a.status, kStatusEmptyTimeout);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        mbar_expect_tx(&full[s], stage_bytes);
+        unsigned char* dst = wst + static_cast<size_t>(s) * W_STAGE_BYTES;
+        if (MODE == MODE_GATEUP) {
+          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * (BR / 2)), &full[s], pol);
+          tma_load_2d(dst + W_STAGE_BYTES / 2, &umap, static_cast<int32_t>(pk * KC),
+                      static_cast<int32_t>(pb * (BR / 2)), &full[s], pol);
+        } else {
+          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * BR), &full[s], pol);
+          tma_load_2d_plain(xst + static_cast<size_t>(s) * X_STAGE_BYTES, &xmap, static_cast<int32_t>(pk * KC), 0,
+                            &full[s]);
+        }
+        if (++pk == a.ks) { pk = 0; ++pb; }
+        issued = it + 1;
+      }
+      // Drain: never leave the CTA with copies still landing in shared memory.
+      for (int64_t it = (issued > S ? issued - S : 0); it < issued; ++it) {
+        if (!mbar_wait(&full[it % S], static_cast<uint32_t>((it / S) & 1))) break;
+      }
     }
-  };
-  auto advance_load = [&]() {
-    ++lt;
-    if (++lk == a.ks) {
-      lk = 0;
-      ++lb;
-      wr0 = wrow(lb, 0, ok0);
-      wr1 = wrow(lb, 1, ok1);
-    }
-  };
-
-  // Prologue part 1: weight prefetch (independent of the previous kernel).
-  int64_t kk_of_stage[D];
-#pragma unroll
-  for (int i = 0; i < D; ++i) {
-    kk_of_stage[i] = lk;
-    if (lt < s1) {
-      load_w(i);
-      advance_load();
-    }
+    grid_dep_launch();
+    return;
   }
 
-  // Everything below may read the previous kernel's outputs.
+  // ================= consumer warps
+  const int g = lane >> 2, q = lane & 3;
   grid_dep_wait();
-
-  if (XS) {
+  if (MODE == MODE_GATEUP) {
     // RMSNorm of the m hidden rows into shared memory, rounded to T
-    // (reference.py:389 rounds `normed` to the activation dtype).
+    // (reference.py:389 rounds `normed` to the activation dtype), stored as
+    // 64-column chunks of [m x 128 B] with the same swizzle as a TMA tile.
     const int nvec = static_cast<int>(a.k / 8);
     for (int mrow = warp; mrow < a.m; mrow += GW) {
       const T* hr = reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride;
@@ -318,168 +462,148 @@ __global__ void __launch_bounds__(GW * 32, 2) gemv_streamk_kernel(const GemvArgs
         load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] = f[e] * inv * wv[e];
-        *reinterpret_cast<uint4*>(xs + mrow * a.xs_pitch + 8 * v) = pack8<T>(o);
+        const int chunk = v >> 3, cc = v & 7;
+        *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 +
+                                  ((cc ^ (mrow & 7)) << 4)) = pack8<T>(o);
       }
     }
-    __syncthreads();
+    // Zero the tail of the last chunk when k is not a multiple of 64.
+    if (a.k % KC) {
+      const int chunk = static_cast<int>(a.k / KC);
+      for (int idx = threadIdx.x; idx < a.m * 8; idx += CONSUMERS) {
+        const int mrow = idx >> 3, cc = idx & 7;
+        if (chunk * KC + cc * 8 >= a.k)
+          *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
+      }
+    }
+    consumer_sync();
   }
   grid_dep_launch();
 
-#pragma unroll
-  for (int i = 0; i < D; ++i) load_x(i, kk_of_stage[i]);
-
-  // -------- main loop
-  int64_t ct = s0, cb = s0 / a.ks, ck = s0 - (s0 / a.ks) * a.ks;
   Acc<NT> acc;
-#pragma unroll
-  for (int t = 0; t < NT; ++t)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc.v[t][e] = 0.f;
-  float sacc[2][MP];  // simt accumulators
+  acc.zero();
+  float sacc[2][MP];
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
     for (int mm = 0; mm < MP; ++mm) sacc[r][mm] = 0.f;
 
-  while (ct < s1) {
+  const int r0 = 16 * warp + g;  // weight rows of this lane in the stage tile: r0, r0 + 8
+  int64_t cb = s0 / a.ks, ck = s0 - (s0 / a.ks) * a.ks;
+  for (int64_t it = 0; it < s1 - s0; ++it) {
+    const int s = static_cast<int>(it % S);
+    if (!mbar_wait(&full[s], static_cast<uint32_t>((it / S) & 1))) {
+      atomicOr(a.status, kStatusFullTimeout);
+      s_abort = 1;
+      return;  // every consumer warp times out on this same stage
+    }
+    const unsigned char* wt = wst + static_cast<size_t>(s) * W_STAGE_BYTES;
+    const uint4 wa0 = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q));
+    const uint4 wa1 = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q + 1));
+    const uint4 wb0 = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q));
+    const uint4 wb1 = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q + 1));
+    if (KIND == 0) {
+      uint4 xa[NT][2];
 #pragma unroll
-    for (int i = 0; i < D; ++i) {
-      if (ct < s1) {
-        // ---- compute stage i (step ct, column block ck)
-        if (KIND == 0) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            mma16816<T>(acc.v[t], ra_[i].x, rb_[i].x, ra_[i].y, rb_[i].y, rx_[i][t].x, rx_[i][t].y);
-            mma16816<T>(acc.v[t], ra_[i].z, rb_[i].z, ra_[i].w, rb_[i].w, rx_[i][t].z, rx_[i][t].w);
-          }
+      for (int t = 0; t < NT; ++t) {
+        const int n = g + 8 * t;
+        if (MODE == MODE_LINEAR) {
+          const unsigned char* xt = xst + static_cast<size_t>(s) * X_STAGE_BYTES;
+          xa[t][0] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q));
+          xa[t][1] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q + 1));
+        } else if (n < a.m) {
+          const unsigned char* xt = xs + (ck * a.m + n) * 128;
+          xa[t][0] = *reinterpret_cast<const uint4*>(xt + (((2 * q) ^ (n & 7)) << 4));
+          xa[t][1] = *reinterpret_cast<const uint4*>(xt + (((2 * q + 1) ^ (n & 7)) << 4));
         } else {
-          const int64_t col = ck * KSTEP + 8 * q;
-          if (col < a.k) {
-            float wa[8], wb[8];
-            unpack8<T>(ra_[i], wa);
-            unpack8<T>(rb_[i], wb);
-#pragma unroll
-            for (int mm = 0; mm < MP; ++mm) {
-              if (mm < a.m) {
-                uint4 xv;
-                if (XS)
-                  xv = lds16(xs + mm * a.xs_pitch + col);
-                else
-                  xv = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.x) + mm * a.sxm + col));
-                float xf[8];
-                unpack8<T>(xv, xf);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  sacc[0][mm] = fmaf(wa[e], xf[e], sacc[0][mm]);
-                  sacc[1][mm] = fmaf(wb[e], xf[e], sacc[1][mm]);
-                }
-              }
-            }
-          }
-        }
-        // ---- refill stage i with the step D ahead
-        if (lt < s1) {
-          const int64_t kk = lk;
-          load_w(i);
-          load_x(i, kk);
-          advance_load();
-        }
-        ++ct;
-        ++ck;
-        // ---- block finished (or range ends): flush
-        if (ck == a.ks || ct == s1) {
-          if (KIND == 1) {
-            // reduce the four q-lanes and move to the C-fragment ownership
-#pragma unroll
-            for (int r = 0; r < 2; ++r)
-#pragma unroll
-              for (int mm = 0; mm < MP; ++mm) {
-                float v = sacc[r][mm];
-                v += __shfl_xor_sync(0xffffffffu, v, 1);
-                v += __shfl_xor_sync(0xffffffffu, v, 2);
-                sacc[r][mm] = v;
-              }
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float v = 0.f;
-#pragma unroll
-                for (int qq = 0; qq < 4; ++qq) {
-                  const int col = 8 * t + 2 * qq + (e & 1);
-                  if (col < MP && qq == q) v = sacc[e >> 1][col];
-                }
-                acc.v[t][e] = v;
-              }
-          }
-          const int64_t blk = cb;
-          const bool covered = (s0 <= blk * a.ks) && (s1 >= (blk + 1) * a.ks);
-          if (covered) {
-            Epilogue<T, NT, MODE>::run(a, blk, acc, xchg);
-          } else {
-            const int slot = (blk == s0 / a.ks) ? 0 : 1;
-            float* sp = a.slots + (c * 2 + slot) * (BR * MT_MAX);
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int r = 16 * warp + g + 8 * h;
-                const int col = 8 * t + 2 * q;
-                *reinterpret_cast<float2*>(sp + r * MT_MAX + col) = make_float2(acc.v[t][2 * h], acc.v[t][2 * h + 1]);
-              }
-            __threadfence();
-            __syncthreads();
-            const int64_t cf = cta_of(blk * a.ks, a.total, G);
-            const int64_t cl = cta_of((blk + 1) * a.ks - 1, a.total, G);
-            if (threadIdx.x == 0) {
-              const int old = atomicAdd(a.counters + blk, 1);
-              s_last = (old == static_cast<int>(cl - cf));
-            }
-            __syncthreads();
-            if (s_last) {
-              __threadfence();
-              Acc<NT> sum;
-#pragma unroll
-              for (int t = 0; t < NT; ++t)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) sum.v[t][e] = 0.f;
-              for (int64_t cc = cf; cc <= cl; ++cc) {
-                const int sl = (blk == range_start(cc, a.total, G) / a.ks) ? 0 : 1;
-                const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-#pragma unroll
-                  for (int h = 0; h < 2; ++h) {
-                    const int r = 16 * warp + g + 8 * h;
-                    const int col = 8 * t + 2 * q;
-                    const float2 v = __ldcg(reinterpret_cast<const float2*>(rp + r * MT_MAX + col));
-                    sum.v[t][2 * h] += v.x;
-                    sum.v[t][2 * h + 1] += v.y;
-                  }
-              }
-              Epilogue<T, NT, MODE>::run(a, blk, sum, xchg);
-              if (threadIdx.x == 0) a.counters[blk] = 0;
-            }
-          }
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc.v[t][e] = 0.f;
-#pragma unroll
-          for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int mm = 0; mm < MP; ++mm) sacc[r][mm] = 0.f;
-          ck = 0;
-          ++cb;
+          xa[t][0] = make_uint4(0, 0, 0, 0);
+          xa[t][1] = make_uint4(0, 0, 0, 0);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      // physical column 16q + 4h + j  <->  logical k of MMA h: (2q, 2q+1, 2q+8, 2q+9)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        mma16816<T>(acc.v[t], wa0.x, wb0.x, wa0.y, wb0.y, xa[t][0].x, xa[t][0].y);
+        mma16816<T>(acc.v[t], wa0.z, wb0.z, wa0.w, wb0.w, xa[t][0].z, xa[t][0].w);
+        mma16816<T>(acc.v[t], wa1.x, wb1.x, wa1.y, wb1.y, xa[t][1].x, xa[t][1].y);
+        mma16816<T>(acc.v[t], wa1.z, wb1.z, wa1.w, wb1.w, xa[t][1].z, xa[t][1].w);
+      }
+    } else {
+      float wf[2][16];
+      unpack8<T>(wa0, wf[0]);
+      unpack8<T>(wa1, wf[0] + 8);
+      unpack8<T>(wb0, wf[1]);
+      unpack8<T>(wb1, wf[1] + 8);
+#pragma unroll
+      for (int mm = 0; mm < MP; ++mm) {
+        if (mm < a.m) {
+          uint4 x0, x1;
+          if (MODE == MODE_LINEAR) {
+            const unsigned char* xt = xst + static_cast<size_t>(s) * X_STAGE_BYTES;
+            x0 = *reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q));
+            x1 = *reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q + 1));
+          } else {
+            const unsigned char* xt = xs + (ck * a.m + mm) * 128;
+            x0 = *reinterpret_cast<const uint4*>(xt + (((2 * q) ^ (mm & 7)) << 4));
+            x1 = *reinterpret_cast<const uint4*>(xt + (((2 * q + 1) ^ (mm & 7)) << 4));
+          }
+          float xf[16];
+          unpack8<T>(x0, xf);
+          unpack8<T>(x1, xf + 8);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            sacc[0][mm] = fmaf(wf[0][e], xf[e], sacc[0][mm]);
+            sacc[1][mm] = fmaf(wf[1][e], xf[e], sacc[1][mm]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // ---- block finished (or range ends): flush
+    ++ck;
+    if (ck == a.ks || it + 1 == s1 - s0) {
+      if (KIND == 1) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int mm = 0; mm < MP; ++mm) {
+            float v = sacc[r][mm];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            sacc[r][mm] = v;
+          }
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float v = 0.f;
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const int col = 8 * t + 2 * qq + (e & 1);
+              if (col < MP && qq == q) v = sacc[e >> 1][col];
+            }
+            acc.v[t][e] = v;
+          }
+      }
+      flush_block<T, NT, MODE>(a, cb, acc, xchg, s0, s1, G, c, &s_last);
+      acc.zero();
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int mm = 0; mm < MP; ++mm) sacc[r][mm] = 0.f;
+      ck = 0;
+      ++cb;
     }
   }
 }
 
 // ------------------------------------------------------------ generic GEMV
-// Any strides, any K: one warp per output row.  Used for layouts the
-// streaming kernel cannot address (transposed weights, K % 8 != 0, ...).
+// Any strides, any K: one warp per output row.  Used for layouts the TMA
+// kernel cannot address (transposed weights, unaligned rows, ...).
 struct GenArgs {
   const void* x;
   int64_t sxm, sxk;
@@ -516,12 +640,11 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const GenArgs a) {
 #pragma unroll
   for (int mm = 0; mm < MT_MAX; ++mm) acc[mm] = warp_sum(acc[mm]);
   if (lane == 0) {
-    float bias = a.bias ? load_as_f32(a.bias, a.bias_dtype, row * a.sbias) : 0.f;
+    const float bias = a.bias ? load_as_f32(a.bias, a.bias_dtype, row * a.sbias) : 0.f;
 #pragma unroll
     for (int mm = 0; mm < MT_MAX; ++mm) {
       if (mm < a.m) {
-        float v = acc[mm];
-        if (a.bias) v += bias;
+        float v = acc[mm] + bias;
         if (a.ra) v += load_as_f32(a.ra, a.ra_dtype, mm * a.srm + row * a.srn);
         static_cast<T*>(a.y)[mm * a.sym + row * a.syn] = from_f32<T>(v);
       }
@@ -530,36 +653,83 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const GenArgs a) {
 }
 
 // ------------------------------------------------------------ host side
-constexpr int kCtasPerSm = 2;
-constexpr int kStages = 4;
-
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-int64_t max_grid() { return static_cast<int64_t>(fd_host::sm_count()) * kCtasPerSm; }
+int64_t max_grid() { return static_cast<int64_t>(fd_host::sm_count()); }
 
-// Workspace: [counters (nblocks ints)] [slots: grid x 2 x BR x MT_MAX floats]
-size_t streamk_ws_bytes(int64_t nblocks) {
-  return align256(static_cast<size_t>(nblocks) * sizeof(int)) +
-         align256(static_cast<size_t>(max_grid()) * 2 * BR * MT_MAX * sizeof(float));
+// Workspace layout (fixed for a device, whatever the shape, so one buffer can
+// serve every launch):  [slots: grid x 2 x BR x MT_MAX floats]
+//                       [counters: kMaxCounters ints][status: 64 ints]
+//                       [MLP intermediate]
+size_t slots_bytes() { return align256(static_cast<size_t>(max_grid()) * 2 * BR * MT_MAX * sizeof(float)); }
+size_t counters_offset() { return slots_bytes(); }
+size_t status_offset() { return counters_offset() + kMaxCounters * sizeof(int); }
+size_t streamk_ws_bytes() { return status_offset() + 256; }
+
+struct Workspace {
+  float* slots;
+  int* counters;
+  int* status;
+  char* tail;
+};
+Workspace carve(void* ws) {
+  char* p = static_cast<char*>(ws);
+  return {reinterpret_cast<float*>(p), reinterpret_cast<int*>(p + counters_offset()),
+          reinterpret_cast<int*>(p + status_offset()), p + streamk_ws_bytes()};
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D map over a [rows, cols] 16-bit matrix with row stride `stride` elements;
+// box = [box_rows x 64 cols], 128B swizzle, out-of-range elements read as 0.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(KC), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+size_t tma_smem_bytes(int mode, int mt, int m, int64_t ks, int stages) {
+  const size_t xbytes = mode == MODE_GATEUP ? static_cast<size_t>(ks) * m * 128
+                                            : static_cast<size_t>(stages) * mt * KC * 2;
+  return 1024 + static_cast<size_t>(stages) * W_STAGE_BYTES + ((xbytes + 15) & ~static_cast<size_t>(15)) +
+         (BR / 2) * MT_MAX * 4 + 2 * MAX_STAGES * 8;
+}
+
+constexpr size_t kSmemLimit = 227 * 1024 - 1024;  // opt-in maximum, less static shared memory
+
+// Largest stage count (<= MAX_STAGES) whose shared memory fits; 0 if none >= 2.
+int pick_stages(int mode, int mt, int m, int64_t ks) {
+  for (int s = MAX_STAGES; s >= 2; --s)
+    if (tma_smem_bytes(mode, mt, m, ks, s) <= kSmemLimit) return s;
+  return 0;
 }
 
 template <typename Kern>
-cudaError_t launch_pdl(Kern kern, int64_t total, size_t smem, cudaStream_t st, const GemvArgs& a) {
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
-  // One wave: as many CTAs as fit at once (at most kCtasPerSm per SM), never
-  // more than there are steps, so every CTA owns a non-empty step range.
-  int occ = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GW * 32, smem);
+cudaError_t launch_tma(Kern kern, const CUtensorMap& wm, const CUtensorMap& um, const CUtensorMap& xm,
+                       const GemvArgs& a, size_t smem, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  occ = std::max(1, std::min(occ, kCtasPerSm));
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(fd_host::sm_count()) * occ, total));
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(max_grid(), a.total));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(GW * 32);
+  cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -567,24 +737,45 @@ cudaError_t launch_pdl(Kern kern, int64_t total, size_t smem, cudaStream_t st, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  return cudaLaunchKernelEx(&cfg, kern, wm, um, xm, a);
 }
 
-template <typename T, int MODE, bool XS>
-cudaError_t launch_streamk(const GemvArgs& a, int kind, size_t smem, cudaStream_t st) {
-  const int64_t grid = a.total;
+template <typename T, int MODE>
+cudaError_t dispatch_tma(const CUtensorMap& wm, const CUtensorMap& um, const CUtensorMap& xm, const GemvArgs& a,
+                         int kind, size_t smem, cudaStream_t st) {
   if (kind == FD_KIND_DOT) {
-    if (a.m <= 8) return launch_pdl(gemv_streamk_kernel<T, 1, 0, 1, MODE, XS, kStages>, grid, smem, st, a);
-    return launch_pdl(gemv_streamk_kernel<T, 2, 0, 1, MODE, XS, kStages>, grid, smem, st, a);
+    if (a.m <= 8) return launch_tma(gemv_tma_kernel<T, 1, 0, 1, MODE>, wm, um, xm, a, smem, st);
+    return launch_tma(gemv_tma_kernel<T, 2, 0, 1, MODE>, wm, um, xm, a, smem, st);
   }
-  if (a.m <= 1) return launch_pdl(gemv_streamk_kernel<T, 1, 1, 1, MODE, XS, kStages>, grid, smem, st, a);
-  if (a.m <= 2) return launch_pdl(gemv_streamk_kernel<T, 1, 1, 2, MODE, XS, kStages>, grid, smem, st, a);
-  if (a.m <= 4) return launch_pdl(gemv_streamk_kernel<T, 1, 1, 4, MODE, XS, kStages>, grid, smem, st, a);
-  if (a.m <= 8) return launch_pdl(gemv_streamk_kernel<T, 1, 1, 8, MODE, XS, kStages>, grid, smem, st, a);
-  return launch_pdl(gemv_streamk_kernel<T, 2, 1, 16, MODE, XS, kStages>, grid, smem, st, a);
+  if (a.m <= 1) return launch_tma(gemv_tma_kernel<T, 1, 1, 1, MODE>, wm, um, xm, a, smem, st);
+  if (a.m <= 2) return launch_tma(gemv_tma_kernel<T, 1, 1, 2, MODE>, wm, um, xm, a, smem, st);
+  if (a.m <= 4) return launch_tma(gemv_tma_kernel<T, 1, 1, 4, MODE>, wm, um, xm, a, smem, st);
+  if (a.m <= 8) return launch_tma(gemv_tma_kernel<T, 1, 1, 8, MODE>, wm, um, xm, a, smem, st);
+  return launch_tma(gemv_tma_kernel<T, 2, 1, 16, MODE>, wm, um, xm, a, smem, st);
 }
 
 int from_cuda(cudaError_t e) { return e == cudaSuccess ? FD_OK : FD_ERR_LAUNCH; }
+
+// Launch the stream-K TMA GEMV in LINEAR mode: y = x @ w^T (+bias)(+row_add).
+int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvArgs a, int dtype, int kind,
+                  const Workspace& ws, cudaStream_t st) {
+  const int mt = a.m <= 8 ? 8 : 16;
+  a.ks = (a.k + KC - 1) / KC;
+  a.nblocks = (a.n + BR - 1) / BR;
+  if (a.nblocks > kMaxCounters) return FD_ERR_UNSUPPORTED;
+  a.total = a.nblocks * a.ks;
+  a.stages = pick_stages(MODE_LINEAR, mt, a.m, a.ks);
+  if (a.stages == 0) return FD_ERR_UNSUPPORTED;
+  a.slots = ws.slots; a.counters = ws.counters; a.status = ws.status;
+  CUtensorMap wm, xm;
+  // A single row's stride is never used by the TMA unit; keep it legal.
+  const int64_t xstride = a.m == 1 ? ((a.k + 7) / 8) * 8 : sxm;
+  if (!make_map(&wm, w, a.n, a.k, swn, BR) || !make_map(&xm, x, a.m, a.k, xstride, mt)) return FD_ERR_LAUNCH;
+  const size_t smem = tma_smem_bytes(MODE_LINEAR, mt, a.m, a.ks, a.stages);
+  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR>(wm, wm, xm, a, kind, smem, st)
+                                   : dispatch_tma<__half, MODE_LINEAR>(wm, wm, xm, a, kind, smem, st);
+  return from_cuda(e);
+}
 
 int check_mlp_args(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
                    int64_t s_gu, int32_t dtype, int32_t m, int64_t h, int64_t i, int32_t kind) {
@@ -594,35 +785,38 @@ int check_mlp_args(const void* hidden, const void* norm_w, int32_t norm_dtype, c
   if (!hidden || !norm_w || !w_gate_up) return FD_ERR_ARG;
   if (!half_dtype(dtype) || !valid_dtype(norm_dtype)) return FD_ERR_ARG;
   if (kind != FD_KIND_DOT && kind != FD_KIND_SIMT) return FD_ERR_ARG;
-  if (h % 8 || i % 8 || i == 0 || s_gu % 8) return FD_ERR_UNSUPPORTED;
+  if (h % 8 || i % 8 || i == 0 || s_gu % 8 || s_gu < h) return FD_ERR_UNSUPPORTED;
   if (!aligned16(hidden) || !aligned16(norm_w) || !aligned16(w_gate_up)) return FD_ERR_UNSUPPORTED;
-  // RMSNorm'd batch lives in shared memory next to the gate/up exchange tile.
-  if (static_cast<size_t>(m) * (h + XPAD / 2) * 2 + static_cast<size_t>(BR / 2) * MT_MAX * sizeof(float) >
-      200 * 1024)
-    return FD_ERR_UNSUPPORTED;
+  const int64_t ks = (h + KC - 1) / KC;
+  if (m > 0 && pick_stages(MODE_GATEUP, m <= 8 ? 8 : 16, m, ks) == 0) return FD_ERR_UNSUPPORTED;
+  if ((i + BR / 2 - 1) / (BR / 2) > kMaxCounters) return FD_ERR_UNSUPPORTED;
   return FD_OK;
 }
 
 // Kernel 1 of the MLP: RMSNorm (prologue) -> gate/up GEMV -> SwiGLU -> mid.
-cudaError_t launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype,
-                           const void* w_gate_up, int64_t s_gu, void* mid, int64_t s_mid,
-                           int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
-                           int* counters, float* slots, cudaStream_t st) {
+int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
+                   int64_t s_gu, void* mid, int64_t s_mid, int32_t dtype, int32_t m, int64_t h, int64_t i,
+                   float eps, int32_t kind, const Workspace& ws, cudaStream_t st) {
   GemvArgs a = {};
-  a.w = static_cast<const char*>(w_gate_up); a.swn = s_gu;
   a.y = static_cast<char*>(mid); a.sym = s_mid; a.syn = 1;
   a.m = m; a.n = 2 * i; a.k = h;
-  a.ks = (h + KSTEP - 1) / KSTEP;
+  a.ks = (h + KC - 1) / KC;
   a.nblocks = (i + BR / 2 - 1) / (BR / 2);
   a.total = a.nblocks * a.ks;
-  a.counters = counters; a.slots = slots;
+  a.slots = ws.slots; a.counters = ws.counters; a.status = ws.status;
   a.inner = i;
   a.hidden = hidden; a.hidden_stride = h;
   a.norm_w = norm_w; a.norm_dtype = norm_dtype; a.eps = eps;
-  a.xs_pitch = static_cast<int32_t>(h + XPAD / 2);  // elements (2-byte types)
-  const size_t smem = static_cast<size_t>(m) * a.xs_pitch * 2 + static_cast<size_t>(BR / 2) * MT_MAX * sizeof(float);
-  return dtype == FD_BF16 ? launch_streamk<__nv_bfloat16, MODE_GATEUP, true>(a, kind, smem, st)
-                          : launch_streamk<__half, MODE_GATEUP, true>(a, kind, smem, st);
+  const int mt = m <= 8 ? 8 : 16;
+  a.stages = pick_stages(MODE_GATEUP, mt, m, a.ks);
+  if (a.stages == 0) return FD_ERR_UNSUPPORTED;
+  CUtensorMap gm, um;
+  const char* up = static_cast<const char*>(w_gate_up) + static_cast<int64_t>(i) * s_gu * 2;
+  if (!make_map(&gm, w_gate_up, i, h, s_gu, BR / 2) || !make_map(&um, up, i, h, s_gu, BR / 2)) return FD_ERR_LAUNCH;
+  const size_t smem = tma_smem_bytes(MODE_GATEUP, mt, m, a.ks, a.stages);
+  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, um, gm, a, kind, smem, st)
+                                   : dispatch_tma<__half, MODE_GATEUP>(gm, um, gm, a, kind, smem, st);
+  return from_cuda(e);
 }
 
 }  // namespace
@@ -631,9 +825,9 @@ extern "C" {
 
 size_t fd_linear_workspace_bytes(int32_t m, int64_t n, int64_t k) {
   (void)m;
+  (void)n;
   (void)k;
-  const int64_t nblocks = (n + BR - 1) / BR;
-  return streamk_ws_bytes(std::max<int64_t>(nblocks, 1));
+  return streamk_ws_bytes();
 }
 
 int fd_linear_out(const void* x, int64_t sxm, int64_t sxk, const void* w, int64_t swn, int64_t swk,
@@ -650,30 +844,19 @@ int fd_linear_out(const void* x, int64_t sxm, int64_t sxk, const void* w, int64_
   if (bias && !(bias_dtype == dtype || bias_dtype == FD_F32)) return FD_ERR_ARG;
   if (row_add && !valid_dtype(ra_dtype)) return FD_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool bf = dtype == FD_BF16;
 
-  const bool fast = k > 0 && swk == 1 && sxk == 1 && k % 8 == 0 && aligned16(x) && aligned16(w) &&
-                    swn % 8 == 0 && (m == 1 || sxm % 8 == 0);
-  if (fast) {
+  // The TMA path needs unit k-strides, 16-byte aligned bases and row strides.
+  const bool tma = k > 0 && swk == 1 && sxk == 1 && aligned16(x) && aligned16(w) && swn % 8 == 0 &&
+                   swn >= k && (m == 1 || (sxm % 8 == 0 && sxm >= k)) && encode_fn() != nullptr;
+  if (tma) {
+    if (!workspace || workspace_bytes < streamk_ws_bytes()) return FD_ERR_WORKSPACE;
     GemvArgs a = {};
-    a.x = static_cast<const char*>(x); a.sxm = sxm;
-    a.w = static_cast<const char*>(w); a.swn = swn;
     a.bias = bias; a.bias_dtype = bias_dtype; a.sbias = sbias;
     a.ra = row_add; a.ra_dtype = ra_dtype; a.srm = srm; a.srn = srn;
     a.y = static_cast<char*>(y); a.sym = sym; a.syn = syn;
     a.m = m; a.n = n; a.k = k;
-    a.ks = (k + KSTEP - 1) / KSTEP;
-    a.nblocks = (n + BR - 1) / BR;
-    a.total = a.nblocks * a.ks;
-    const size_t need = streamk_ws_bytes(a.nblocks);
-    if (!workspace || workspace_bytes < need) return FD_ERR_WORKSPACE;
-    a.counters = static_cast<int*>(workspace);
-    a.slots = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                       align256(static_cast<size_t>(a.nblocks) * sizeof(int)));
-    const size_t smem = 0;
-    cudaError_t e = bf ? launch_streamk<__nv_bfloat16, MODE_LINEAR, false>(a, kind, smem, st)
-                       : launch_streamk<__half, MODE_LINEAR, false>(a, kind, smem, st);
-    return from_cuda(e);
+    const int r = launch_linear(x, sxm, w, swn, a, dtype, kind, carve(workspace), st);
+    if (r != FD_ERR_UNSUPPORTED) return r;
   }
   GenArgs a;
   a.x = x; a.sxm = sxm; a.sxk = sxk;
@@ -684,20 +867,17 @@ int fd_linear_out(const void* x, int64_t sxm, int64_t sxk, const void* w, int64_
   a.m = m; a.n = n; a.k = k;
   const int64_t threads = n * 32;
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  if (bf) gemv_generic_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
+  if (dtype == FD_BF16) gemv_generic_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
   else gemv_generic_kernel<__half><<<blocks, 256, 0, st>>>(a);
   return from_cuda(cudaGetLastError());
 }
 
-// Fused post-attention MLP.  Workspace layout:
-//   [counters: max(nblocks_gu, nblocks_down) ints][slots][mid: m x i of T]
 size_t fd_post_attn_mlp_workspace_bytes(int32_t m, int64_t h, int64_t i) {
-  const int64_t nb_gu = (i + BR / 2 - 1) / (BR / 2);
-  const int64_t nb_dn = (h + BR - 1) / BR;
-  const int64_t nb = std::max<int64_t>(1, std::max(nb_gu, nb_dn));
-  return streamk_ws_bytes(nb) + align256(static_cast<size_t>(std::max(m, 1)) * i * 2);
+  (void)h;
+  return streamk_ws_bytes() + align256(static_cast<size_t>(std::max(m, 1)) * i * 2);
 }
 
+size_t fd_workspace_status_offset(void) { return status_offset(); }
 
 int fd_mlp_gate_up_out(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
                        int64_t s_gu, void* mid, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps,
@@ -705,13 +885,11 @@ int fd_mlp_gate_up_out(const void* hidden, const void* norm_w, int32_t norm_dtyp
   const int chk = check_mlp_args(hidden, norm_w, norm_dtype, w_gate_up, s_gu, dtype, m, h, i, kind);
   if (chk != FD_OK) return chk;
   if (m == 0 || h == 0) return FD_OK;
-  if (!mid) return FD_ERR_ARG;
-  const int64_t nb = (i + BR / 2 - 1) / (BR / 2);
-  if (!workspace || workspace_bytes < streamk_ws_bytes(nb)) return FD_ERR_WORKSPACE;
-  int* counters = static_cast<int*>(workspace);
-  float* slots = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(static_cast<size_t>(nb) * sizeof(int)));
-  return from_cuda(launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, i, dtype, m, h, i, eps,
-                                  kind, counters, slots, static_cast<cudaStream_t>(stream)));
+  if (!mid || !fd_host::aligned16(mid)) return FD_ERR_ARG;
+  if (!workspace || workspace_bytes < streamk_ws_bytes()) return FD_ERR_WORKSPACE;
+  if (!encode_fn()) return FD_ERR_DEVICE;
+  return launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, i, dtype, m, h, i, eps, kind,
+                        carve(workspace), static_cast<cudaStream_t>(stream));
 }
 
 int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
@@ -724,38 +902,23 @@ int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dt
   if (m == 0 || h == 0) return FD_OK;
   if (!w_down || !out) return FD_ERR_ARG;
   if (!(out_dtype == dtype || out_dtype == FD_F32)) return FD_ERR_ARG;
-  if (s_down % 8 || !aligned16(w_down) || !aligned16(out)) return FD_ERR_UNSUPPORTED;
-  const size_t need = fd_post_attn_mlp_workspace_bytes(m, h, i);
-  if (!workspace || workspace_bytes < need) return FD_ERR_WORKSPACE;
+  if (s_down % 8 || s_down < i || !aligned16(w_down) || !aligned16(out)) return FD_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < fd_post_attn_mlp_workspace_bytes(m, h, i)) return FD_ERR_WORKSPACE;
+  if (!encode_fn()) return FD_ERR_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Workspace ws = carve(workspace);
+  char* mid = ws.tail;
 
-  const int64_t nb_gu = (i + BR / 2 - 1) / (BR / 2);
-  const int64_t nb_dn = (h + BR - 1) / BR;
-  const int64_t nb = std::max(nb_gu, nb_dn);
-  char* ws = static_cast<char*>(workspace);
-  int* counters = reinterpret_cast<int*>(ws);
-  float* slots = reinterpret_cast<float*>(ws + align256(static_cast<size_t>(nb) * sizeof(int)));
-  char* mid = ws + streamk_ws_bytes(nb);
-
-  cudaError_t e = launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, i, dtype, m, h, i, eps,
-                                 kind, counters, slots, st);
-  if (e != cudaSuccess) return FD_ERR_LAUNCH;
+  int r = launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, i, dtype, m, h, i, eps, kind, ws, st);
+  if (r != FD_OK) return r;
 
   // Kernel 2: down GEMV (+ residual) -> out [m, h].
   GemvArgs b = {};
-  b.x = mid; b.sxm = i;
-  b.w = static_cast<const char*>(w_down); b.swn = s_down;
   b.ra = add_residual ? hidden : nullptr; b.ra_dtype = dtype; b.srm = h; b.srn = 1;
   b.y = static_cast<char*>(out); b.sym = h; b.syn = 1;
   b.y_f32 = out_dtype == FD_F32;
   b.m = m; b.n = h; b.k = i;
-  b.ks = (i + KSTEP - 1) / KSTEP;
-  b.nblocks = nb_dn;
-  b.total = b.nblocks * b.ks;
-  b.counters = counters; b.slots = slots;
-  e = dtype == FD_BF16 ? launch_streamk<__nv_bfloat16, MODE_LINEAR, false>(b, kind, 0, st)
-                       : launch_streamk<__half, MODE_LINEAR, false>(b, kind, 0, st);
-  return from_cuda(e);
+  return launch_linear(mid, i, w_down, s_down, b, dtype, kind, ws, st);
 }
 
 }  // extern "C"

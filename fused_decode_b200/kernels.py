@@ -107,6 +107,19 @@ class _WorkspaceCache:
     def clear(self) -> None:
         self._bufs.clear()
 
+    def status(self) -> dict:
+        """Error bits of every cached workspace (synchronises the device).
+
+        Non-zero means a kernel's bounded shared-memory pipeline wait expired
+        (1: consumer, 2: producer) and its output is not valid.
+        """
+        off = _capi.load().fd_workspace_status_offset()
+        out = {}
+        for key, buf in self._bufs.items():
+            if buf.numel() >= off + 4:
+                out[key] = int(buf[off:off + 4].view(torch.int32).item())
+        return out
+
 
 WORKSPACES = _WorkspaceCache()
 

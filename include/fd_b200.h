@@ -89,10 +89,17 @@ int fd_swiglu_out(const fd_rows* gate, const fd_rows* up, const fd_rows* out,
 int fd_rope_out(const fd_rows* x, const fd_rows* cos, const fd_rows* sin,
                 const fd_rows* out, void* stream);
 
-/* Workspace bytes fd_linear_out needs for this shape (0 if none).  The
- * workspace must be zero-filled once when first allocated; every launch
- * leaves it zeroed again. */
+/* Workspace bytes fd_linear_out needs for this shape.  The workspace must be
+ * zero-filled once when first allocated; every launch leaves its counters at
+ * zero again, so one buffer serves every later launch on the same stream
+ * (launches that share a workspace must not overlap in time). */
 size_t fd_linear_workspace_bytes(int32_t m, int64_t n, int64_t k);
+
+/* Byte offset, inside any workspace above, of a 32-bit status word the
+ * kernels OR error bits into (1: a consumer's shared-memory pipeline wait
+ * expired, 2: a producer's wait expired).  Zero means no error; the caller
+ * resets it. */
+size_t fd_workspace_status_offset(void);
 
 /* y[m, n] = round(sum_k x[m, k] * w[n, k] + bias[n] + row_add[m, n]) for
  * 1 <= m <= 16, fp32 accumulation.  bias (dtype = x dtype or f32) and row_add

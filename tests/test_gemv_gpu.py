@@ -203,3 +203,9 @@ def test_mlp_fallback_layout():
     x = torch.randn(m, h, device="cuda", dtype=torch.float16, generator=_gen(4))
     ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-6, "float16")
     _close(post_attn_mlp(x, nw, wgu, wd_t, kind="dot"), ref)
+
+
+def test_zz_no_pipeline_timeouts():
+    """No kernel in this module hit a bounded pipeline wait."""
+    torch.cuda.synchronize()
+    assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
