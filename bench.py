@@ -444,6 +444,69 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+NCU_CASES = ("gate_up", "down", "mlp", "add_rms", "rms", "swiglu", "rope", "copy")
+
+
+def run_ncu_case(args) -> None:
+    """A small fixed workload for an ncu capture: 2 warm-up launches, then 3
+    launches of the named kernel (one layer, Llama-3-8B widths, M = --m).
+    Prints nothing but a one-line summary; never used for timing."""
+    import torch
+
+    import fused_decode_b200 as fd
+    from fused_decode_b200 import _capi
+    from fused_decode_b200 import kernels as K
+
+    _capi.load()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    m, bf = args.m, torch.bfloat16
+    case = args.ncu_case
+    if case in ("gate_up", "down", "mlp"):
+        (nw, wgu, wd), = make_layers(torch, dev, 1)
+        x = torch.randn(m, H, device=dev, dtype=bf, generator=g)
+        mid = torch.randn(m, I, device=dev, dtype=bf, generator=g)
+        y = torch.empty(m, H, device=dev, dtype=bf)
+        fn = {
+            "gate_up": lambda: K.mlp_gate_up_out(x, nw, wgu, mid, EPS, "dot"),
+            "down": lambda: K.linear_out(mid, wd, y, row_add=x, kind="dot"),
+            "mlp": lambda: fd.post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot"),
+        }[case]
+    elif case in ("add_rms", "rms"):
+        x = torch.randn(8192, H, device=dev, dtype=torch.float16, generator=g)
+        r = torch.randn(8192, H, device=dev, dtype=torch.float16, generator=g)
+        w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half()
+        out = torch.empty_like(x)
+        fn = ((lambda: fd.add_rms_norm(x, r, w, 1e-5, out=out, residual_out=r)) if case == "add_rms"
+              else (lambda: fd.rms_norm(x, w, 1e-5, out=out)))
+    elif case == "swiglu":
+        a = torch.randn(2048, I, device=dev, dtype=torch.float16, generator=g)
+        b = torch.randn(2048, I, device=dev, dtype=torch.float16, generator=g)
+        out = torch.empty_like(a)
+        fn = lambda: fd.swiglu(a, b, out=out)  # noqa: E731
+    elif case == "rope":
+        x = torch.randn(1, 2048, 32, 128, device=dev, dtype=torch.float16, generator=g)
+        cos, sin = rope_tables(torch, 2048, 128, dev, torch.float16)
+        out = torch.empty_like(x)
+        fn = lambda: fd.rope(x, cos, sin, out=out)  # noqa: E731
+    else:
+        a = torch.empty(1 << 28, device=dev, dtype=bf).normal_()
+        b = torch.empty_like(a)
+        fn = lambda: K.launch_copy(b, a)  # noqa: E731
+    for _ in range(5):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_case": case, "m": m, "launches": 5}))
+
+
+def rope_tables(torch, positions, dim, device, dtype, theta=500000.0):
+    """cos/sin [positions, 1, dim] for rotate-half RoPE: inv_freq[j] = theta^(-2j/dim)."""
+    inv = theta ** (-torch.arange(0, dim, 2, dtype=torch.float32, device=device) / dim)
+    f = torch.outer(torch.arange(positions, dtype=torch.float32, device=device), inv)
+    emb = torch.cat((f, f), dim=-1)
+    return emb.cos().to(dtype).view(positions, 1, dim), emb.sin().to(dtype).view(positions, 1, dim)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -453,7 +516,12 @@ def main() -> None:
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ncu-case", choices=NCU_CASES, default=None,
+                    help="run a small fixed workload of one kernel for an ncu capture and exit")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case(args)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

@@ -2,23 +2,26 @@
 //
 // Design (sm_100a, HBM-bound: a weight byte is used 2*M times):
 //  * Stream-K over the weight.  The weight is cut into blocks of 128 rows; a
-//    block is a run of KS steps of 64 columns.  The grid (one CTA per SM)
-//    splits the flat step range [0, nblocks*KS) into equal contiguous pieces,
-//    so every SM streams the same number of weight bytes whatever N and K are.
-//    (The reference launches cdiv(N, 64) CTAs with no split-K, kernels.py:775,
-//    which leaves most of 148 SMs idle at N = 4096.)
-//  * TMA pipeline.  A producer warp issues 2-D tensor-map loads
-//    (cp.async.bulk.tensor, 128-byte swizzle) of each step's [128 x 64] weight
-//    tile -- and, for a plain GEMV, the [M x 64] activation tile -- into an
-//    S-stage shared-memory ring guarded by mbarriers.  Out-of-range rows and
-//    columns are zero-filled by the TMA unit, so ragged N and K need no masks.
+//    block is a run of KS steps of B x 64 columns.  The grid (one or two CTAs
+//    per SM) splits the flat step range [0, nblocks*KS) into equal contiguous
+//    pieces, so every SM streams the same number of weight bytes whatever N
+//    and K are.  (The reference launches cdiv(N, 64) CTAs with no split-K,
+//    kernels.py:775, which leaves most of 148 SMs idle at N = 4096.)
+//  * TMA pipeline.  P producer warps take turns issuing each step's B 2-D
+//    tensor-map loads (cp.async.bulk.tensor, 128-byte swizzle) of a
+//    [128 x 64] weight box -- and, for a plain GEMV, the [M x 64] activation
+//    boxes -- into an S-stage shared-memory ring guarded by mbarriers.
+//    Measured on B200: a single issuing thread keeps only about two stages in
+//    flight, so several producers (or two CTAs per SM) are what let large
+//    16 KB boxes saturate HBM.  Out-of-range rows and columns are zero-filled
+//    by the TMA unit.
 //  * Eight consumer warps own 16 weight rows each.  "dot" kind: each lane
 //    reads 16 contiguous columns of its two rows (rows g and g+8, g = lane/4,
 //    q = lane%4) -- conflict-free under the 128B swizzle -- and feeds four
-//    mma.sync m16n8k16 per step (swap-AB: weight = A, batch = N of 8 or 16).
-//    The physical columns a lane holds are assigned to logical MMA k-indices
-//    by one fixed permutation applied to both A and B, so the sum is exact.
-//    "simt" kind: the same tiles, fp32 FMAs against all M rows.
+//    mma.sync m16n8k16 per box (swap-AB: weight = A, batch = N of 8 or 16).
+//    The physical columns a lane holds map to logical MMA k-indices by one
+//    fixed permutation applied to both A and B, so the sum is exact.  "simt"
+//    kind: the same tiles, fp32 FMAs against all M rows.
 //  * Split-K partials go to per-CTA slots in a caller workspace; the last CTA
 //    to finish a block (an atomic counter) sums the slots in CTA order --
 //    deterministic, no inter-CTA waiting -- applies the epilogue and re-zeroes
@@ -26,32 +29,35 @@
 //  * Every mbarrier wait is bounded (globaltimer, 2 s): on expiry the CTA sets
 //    a bit in the workspace status word and leaves instead of hanging.
 //  * The MLP gate/up kernel computes RMSNorm of the (tiny) hidden batch into
-//    shared memory in its prologue, pairs 64 gate rows with the matching 64 up
-//    rows in each block and applies SwiGLU in the epilogue; the down kernel
-//    adds the residual in its epilogue.  Kernels launch with programmatic
-//    dependent launch: the weight prefetch is issued before griddepcontrol.wait.
+//    shared memory in its prologue; each 128-row block is 64 gate rows over
+//    the matching 64 up rows (one 3-D box), so SwiGLU is a local epilogue.
+//    The down kernel adds the residual in its epilogue.  Kernels launch with
+//    programmatic dependent launch: the weight prefetch is issued before
+//    griddepcontrol.wait.
 #include "fd_common.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 
 using namespace fd;
 
 namespace {
 
-constexpr int GW = 8;             // consumer warps per CTA
-constexpr int BR = GW * 16;       // weight rows per block
-constexpr int KC = 64;            // columns per step (128 bytes of a 16-bit row)
-constexpr int MT_MAX = 16;        // max batch rows
+constexpr int GW = 8;                      // consumer warps per CTA
+constexpr int BR = GW * 16;                // weight rows per block
+constexpr int KC = 64;                     // columns per box (128 bytes of a 16-bit row)
+constexpr int BOX_BYTES = BR * KC * 2;     // 16 KB weight box
+constexpr int MAX_BOXES = 2;               // boxes per stage
+constexpr int MT_MAX = 16;                 // max batch rows
 constexpr int CONSUMERS = GW * 32;
-constexpr int THREADS = CONSUMERS + 32;  // + one producer warp
-constexpr int W_STAGE_BYTES = BR * KC * 2;  // 16 KB
-constexpr int MAX_STAGES = 8;
-constexpr int64_t kMaxCounters = 1 << 16;   // blocks per launch (N <= 8M rows)
-constexpr uint64_t kWaitNs = 2000000000ull; // bounded mbarrier waits: 2 s
+constexpr int MAX_PRODUCERS = 3;
+constexpr int MAX_STAGES = 12;
+constexpr int64_t kMaxCounters = 1 << 16;  // blocks per launch (N <= 8M rows)
+constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s
 
 // Status bits written to the workspace status word.
 constexpr int kStatusFullTimeout = 1;
@@ -75,12 +81,14 @@ struct GemvArgs {
   int64_t ks;       // steps per block
   int64_t nblocks;
   int64_t total;    // nblocks * ks
-  int32_t stages;
+  int32_t stages;   // S
+  int32_t boxes;    // B: 64-column boxes per step
+  int32_t x_slot;   // LINEAR: bytes per activation box slot (1024-aligned)
   float* slots;     // [grid][2][BR * MT_MAX]
   int* counters;    // [nblocks]
   int* status;      // error bits
   // gate/up mode
-  int64_t inner;            // I: up rows start at row I of w
+  int64_t inner;            // I: number of gate (= up) rows
   const void* hidden;       // [m, k] rows, row stride hidden_stride
   int64_t hidden_stride;
   const void* norm_w;
@@ -153,13 +161,22 @@ FD_DEV uint64_t evict_first_policy() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-// 2-D tiled TMA load into this CTA's shared memory, completing on `bar`.
+// 2-D / 3-D tiled TMA loads into this CTA's shared memory, completing on `bar`
+// (no multicast: every CTA fetches its own tiles).
 FD_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar,
                         uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
       "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+FD_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z, uint64_t* bar,
+                        uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
 FD_DEV void tma_load_2d_plain(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
@@ -332,30 +349,34 @@ FD_DEV void flush_block(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, floa
 
 // ------------------------------------------------------------ the TMA kernel
 // KIND 0 = dot (mma.sync), 1 = simt.  MP = padded batch for simt (1..16).
-// NT * 8 = batch rows of the activation tile (8 or 16).
-template <typename T, int NT, int KIND, int MP, int MODE>
-__global__ void __launch_bounds__(THREADS, 1)
-    gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
-                    const __grid_constant__ CUtensorMap xmap, const GemvArgs a) {
-  constexpr int MT = NT * 8;
-  constexpr int X_STAGE_BYTES = MT * KC * 2;
+// NT = number of 8-wide MMA batch tiles (1 for m <= 8, 2 for m <= 16).
+// MAXT / MINB: launch bounds (threads, resident CTAs per SM).
+template <typename T, int NT, int KIND, int MP, int MODE, int MAXT, int MINB>
+__global__ void __launch_bounds__(MAXT, MINB)
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                    const GemvArgs a) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ int s_last;
   __shared__ int s_abort;
+  __shared__ float s_sumsq[GW][MT_MAX];
   // 1024-byte alignment for the 128B swizzle atoms.
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
   const int S = a.stages;
-  unsigned char* wst = smem;                                          // S x 16 KB
-  unsigned char* xst = wst + static_cast<size_t>(S) * W_STAGE_BYTES;  // LINEAR: S x MT x 128 B
-  // GATEUP: normed x, ceil(k/64) chunks of [m rows x 128 B], swizzled like a TMA tile
+  const int B = a.boxes;
+  const int x_slot = a.x_slot;
+  const int64_t w_stage = static_cast<int64_t>(B) * BOX_BYTES;
+  unsigned char* wst = smem;                                  // S x B x 16 KB
+  unsigned char* xst = wst + S * w_stage;                     // LINEAR: S x B x x_slot
+  // GATEUP: normed x as 64-column chunks of [m rows x 128 B], swizzled like a TMA tile
   unsigned char* xs = xst;
-  const int64_t xs_bytes = MODE == MODE_GATEUP ? a.ks * a.m * 128 : static_cast<int64_t>(S) * X_STAGE_BYTES;
-  float* xchg = reinterpret_cast<float*>(xst + ((xs_bytes + 15) & ~15ll));
+  const int64_t x_bytes = MODE == MODE_GATEUP ? a.ks * B * a.m * 128 : static_cast<int64_t>(S) * B * x_slot;
+  float* xchg = reinterpret_cast<float*>(xst + ((x_bytes + 15) & ~15ll));
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(xchg) + (BR / 2) * MT_MAX * 4);
   uint64_t* empty = full + MAX_STAGES;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = static_cast<int>(blockDim.x >> 5) - GW;
   const int64_t G = gridDim.x, c = blockIdx.x;
   const int64_t s0 = range_start(c, a.total, G);
   const int64_t s1 = range_start(c + 1, a.total, G);
@@ -370,43 +391,53 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   __syncthreads();
 
-  if (warp == GW) {
-    // ================= producer warp (one lane issues every copy)
+  if (warp >= GW) {
+    // ================= producer warps: producer p issues steps p, p+P, ...
+    const int p = warp - GW;
     if (lane == 0) {
       prefetch_map(&wmap);
-      if (MODE == MODE_GATEUP) prefetch_map(&umap);
-      else prefetch_map(&xmap);
+      if (MODE == MODE_LINEAR) prefetch_map(&xmap);
       const uint64_t pol = evict_first_policy();
-      const uint32_t stage_bytes = W_STAGE_BYTES + (MODE == MODE_LINEAR ? X_STAGE_BYTES : 0);
-      const int64_t b0 = s0 / a.ks, k0 = s0 - (s0 / a.ks) * a.ks;
+      const uint32_t stage_bytes =
+          static_cast<uint32_t>(w_stage) + (MODE == MODE_LINEAR ? static_cast<uint32_t>(B * a.m * 128) : 0u);
       const int64_t n_steps = s1 - s0;
+      auto issue_w = [&](int64_t it) {
+        const int64_t t = s0 + it;
+        const int64_t b = t / a.ks, kk = t - (t / a.ks) * a.ks;
+        const int s = static_cast<int>(it % S);
+        unsigned char* dst = wst + s * w_stage;
+        for (int j = 0; j < B; ++j) {
+          const int32_t col = static_cast<int32_t>((kk * B + j) * KC);
+          if (MODE == MODE_GATEUP)
+            tma_load_3d(dst + j * BOX_BYTES, &wmap, col, static_cast<int32_t>(b * (BR / 2)), 0, &full[s], pol);
+          else
+            tma_load_2d(dst + j * BOX_BYTES, &wmap, col, static_cast<int32_t>(b * BR), &full[s], pol);
+        }
+      };
+      auto issue_x = [&](int64_t it) {
+        const int64_t t = s0 + it;
+        const int64_t kk = t - (t / a.ks) * a.ks;
+        const int s = static_cast<int>(it % S);
+        for (int j = 0; j < B; ++j)
+          tma_load_2d_plain(xst + (s * B + j) * x_slot, &xmap, static_cast<int32_t>((kk * B + j) * KC), 0, &full[s]);
+      };
       const int64_t npre = n_steps < S ? n_steps : S;
       // (1) weight tiles of the first stages: independent of the previous kernel
-      int64_t pb = b0, pk = k0;
-      for (int64_t it = 0; it < npre; ++it) {
+      for (int64_t it = p; it < npre; it += P) {
         mbar_expect_tx(&full[it], stage_bytes);
-        unsigned char* dst = wst + it * W_STAGE_BYTES;
-        if (MODE == MODE_GATEUP) {
-          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * (BR / 2)), &full[it], pol);
-          tma_load_2d(dst + W_STAGE_BYTES / 2, &umap, static_cast<int32_t>(pk * KC),
-                      static_cast<int32_t>(pb * (BR / 2)), &full[it], pol);
-        } else {
-          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * BR), &full[it], pol);
-        }
-        if (++pk == a.ks) { pk = 0; ++pb; }
+        issue_w(it);
       }
       // (2) activation tiles read the previous kernel's output
       if (MODE == MODE_LINEAR) {
         grid_dep_wait();
-        int64_t xb = b0, xk = k0;
-        for (int64_t it = 0; it < npre; ++it) {
-          tma_load_2d_plain(xst + it * X_STAGE_BYTES, &xmap, static_cast<int32_t>(xk * KC), 0, &full[it]);
-          if (++xk == a.ks) { xk = 0; ++xb; }
-        }
+        for (int64_t it = p; it < npre; it += P) issue_x(it);
       }
       // (3) steady state: refill a stage once all consumer warps released it
-      int64_t issued = npre;
-      for (int64_t it = npre; it < n_steps; ++it) {
+      int64_t last = -1;
+      for (int64_t it = p; it < npre; it += P) last = it;
+      int64_t it = p;
+      while (it < npre) it += P;
+      for (; it < n_steps; it += P) {
         const int s = static_cast<int>(it % S);
         if (!mbar_wait(&empty[s], static_cast<uint32_t>((it / S - 1) & 1))) {
           atomicOr(a.status, kStatusEmptyTimeout);
@@ -414,22 +445,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (*reinterpret_cast<volatile int*>(&s_abort)) break;
         mbar_expect_tx(&full[s], stage_bytes);
-        unsigned char* dst = wst + static_cast<size_t>(s) * W_STAGE_BYTES;
-        if (MODE == MODE_GATEUP) {
-          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * (BR / 2)), &full[s], pol);
-          tma_load_2d(dst + W_STAGE_BYTES / 2, &umap, static_cast<int32_t>(pk * KC),
-                      static_cast<int32_t>(pb * (BR / 2)), &full[s], pol);
-        } else {
-          tma_load_2d(dst, &wmap, static_cast<int32_t>(pk * KC), static_cast<int32_t>(pb * BR), &full[s], pol);
-          tma_load_2d_plain(xst + static_cast<size_t>(s) * X_STAGE_BYTES, &xmap, static_cast<int32_t>(pk * KC), 0,
-                            &full[s]);
-        }
-        if (++pk == a.ks) { pk = 0; ++pb; }
-        issued = it + 1;
+        issue_w(it);
+        if (MODE == MODE_LINEAR) issue_x(it);
+        last = it;
       }
-      // Drain: never leave the CTA with copies still landing in shared memory.
-      for (int64_t it = (issued > S ? issued - S : 0); it < issued; ++it) {
-        if (!mbar_wait(&full[it % S], static_cast<uint32_t>((it / S) & 1))) break;
+      // Drain: never leave the CTA with this producer's copies still landing.
+      // Only the last S steps are checked: their stages are never refilled,
+      // so their phase parity is unambiguous.
+      for (int64_t d = last; d >= 0 && d >= n_steps - S; d -= P) {
+        if (!mbar_wait(&full[d % S], static_cast<uint32_t>((d / S) & 1))) break;
       }
     }
     grid_dep_launch();
@@ -438,43 +462,68 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   // ================= consumer warps
   const int g = lane >> 2, q = lane & 3;
+  const int tid = threadIdx.x;
   grid_dep_wait();
   if (MODE == MODE_GATEUP) {
     // RMSNorm of the m hidden rows into shared memory, rounded to T
     // (reference.py:389 rounds `normed` to the activation dtype), stored as
-    // 64-column chunks of [m x 128 B] with the same swizzle as a TMA tile.
+    // 64-column chunks of [m x 128 B] with the same swizzle as a TMA tile;
+    // columns past k (up to the end of the last step) are zero.
     const int nvec = static_cast<int>(a.k / 8);
-    for (int mrow = warp; mrow < a.m; mrow += GW) {
-      const T* hr = reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride;
-      float ss = 0.f;
-      for (int v = lane; v < nvec; v += 32) {
-        float f[8];
-        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(hr) + v), f);
+    const int nvec_pad = static_cast<int>(a.ks * B * (KC / 8));
+    float ss[MT_MAX];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
-      }
-      ss = warp_sum(ss);
-      const float inv = 1.0f / sqrtf(ss / static_cast<float>(a.k) + a.eps);
-      const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
-      for (int v = lane; v < nvec; v += 32) {
-        float f[8], wv[8], o[8];
-        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(hr) + v), f);
-        load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
+    for (int mrow = 0; mrow < MT_MAX; ++mrow) ss[mrow] = 0.f;
+    for (int v = tid; v < nvec; v += CONSUMERS) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = f[e] * inv * wv[e];
-        const int chunk = v >> 3, cc = v & 7;
-        *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 +
-                                  ((cc ^ (mrow & 7)) << 4)) = pack8<T>(o);
+      for (int mrow = 0; mrow < MT_MAX; ++mrow) {
+        if (mrow < a.m) {
+          const uint4* hr =
+              reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride);
+          float f[8];
+          unpack8<T>(__ldg(hr + v), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss[mrow] += f[e] * f[e];
+        }
       }
     }
-    // Zero the tail of the last chunk when k is not a multiple of 64.
-    if (a.k % KC) {
-      const int chunk = static_cast<int>(a.k / KC);
-      for (int idx = threadIdx.x; idx < a.m * 8; idx += CONSUMERS) {
-        const int mrow = idx >> 3, cc = idx & 7;
-        if (chunk * KC + cc * 8 >= a.k)
-          *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4)) =
-              make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int mrow = 0; mrow < MT_MAX; ++mrow) {
+      if (mrow < a.m) {
+        const float t = warp_sum(ss[mrow]);
+        if (lane == 0) s_sumsq[warp][mrow] = t;
+      }
+    }
+    consumer_sync();
+    float inv[MT_MAX];
+#pragma unroll
+    for (int mrow = 0; mrow < MT_MAX; ++mrow) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < GW; ++w) tot += mrow < a.m ? s_sumsq[w][mrow] : 0.f;
+      inv[mrow] = 1.0f / sqrtf(tot / static_cast<float>(a.k) + a.eps);
+    }
+    const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
+    for (int v = tid; v < nvec_pad; v += CONSUMERS) {
+      const int chunk = v >> 3, cc = v & 7;
+      float wv[8];
+      if (v < nvec) load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
+#pragma unroll
+      for (int mrow = 0; mrow < MT_MAX; ++mrow) {
+        if (mrow < a.m) {
+          uint4 packed = make_uint4(0, 0, 0, 0);
+          if (v < nvec) {
+            const uint4* hr =
+                reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride);
+            float f[8], o[8];
+            unpack8<T>(__ldg(hr + v), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = f[e] * inv[mrow] * wv[e];
+            packed = pack8<T>(o);
+          }
+          *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 +
+                                    ((cc ^ (mrow & 7)) << 4)) = packed;
+        }
       }
     }
     consumer_sync();
@@ -489,7 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
     for (int mm = 0; mm < MP; ++mm) sacc[r][mm] = 0.f;
 
-  const int r0 = 16 * warp + g;  // weight rows of this lane in the stage tile: r0, r0 + 8
+  const int r0 = 16 * warp + g;  // weight rows of this lane in every box: r0, r0 + 8
   int64_t cb = s0 / a.ks, ck = s0 - (s0 / a.ks) * a.ks;
   for (int64_t it = 0; it < s1 - s0; ++it) {
     const int s = static_cast<int>(it % S);
@@ -498,65 +547,77 @@ __global__ void __launch_bounds__(THREADS, 1)
       s_abort = 1;
       return;  // every consumer warp times out on this same stage
     }
-    const unsigned char* wt = wst + static_cast<size_t>(s) * W_STAGE_BYTES;
-    const uint4 wa0 = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q));
-    const uint4 wa1 = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q + 1));
-    const uint4 wb0 = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q));
-    const uint4 wb1 = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q + 1));
-    if (KIND == 0) {
-      uint4 xa[NT][2];
+    uint4 wa[MAX_BOXES][2], wb[MAX_BOXES][2];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const int n = g + 8 * t;
-        if (MODE == MODE_LINEAR) {
-          const unsigned char* xt = xst + static_cast<size_t>(s) * X_STAGE_BYTES;
-          xa[t][0] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q));
-          xa[t][1] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q + 1));
-        } else if (n < a.m) {
-          const unsigned char* xt = xs + (ck * a.m + n) * 128;
-          xa[t][0] = *reinterpret_cast<const uint4*>(xt + (((2 * q) ^ (n & 7)) << 4));
-          xa[t][1] = *reinterpret_cast<const uint4*>(xt + (((2 * q + 1) ^ (n & 7)) << 4));
-        } else {
-          xa[t][0] = make_uint4(0, 0, 0, 0);
-          xa[t][1] = make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < MAX_BOXES; ++j) {
+      if (j < B) {
+        const unsigned char* wt = wst + s * w_stage + j * BOX_BYTES;
+        wa[j][0] = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q));
+        wa[j][1] = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q + 1));
+        wb[j][0] = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q));
+        wb[j][1] = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q + 1));
+      }
+    }
+    // activation box j of this step: [m rows x 128 B] (swizzled by row & 7)
+    auto xbox = [&](int j) -> const unsigned char* {
+      return MODE == MODE_LINEAR ? xst + (s * B + j) * x_slot : xs + ((ck * B + j) * a.m) * 128;
+    };
+    if (KIND == 0) {
+      uint4 xa[MAX_BOXES][NT][2];
+#pragma unroll
+      for (int j = 0; j < MAX_BOXES; ++j) {
+        if (j < B) {
+          const unsigned char* xt = xbox(j);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const int n = g + 8 * t;
+            if (n < a.m) {
+              xa[j][t][0] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q));
+              xa[j][t][1] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q + 1));
+            } else {
+              xa[j][t][0] = make_uint4(0, 0, 0, 0);
+              xa[j][t][1] = make_uint4(0, 0, 0, 0);
+            }
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
       // physical column 16q + 4h + j  <->  logical k of MMA h: (2q, 2q+1, 2q+8, 2q+9)
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        mma16816<T>(acc.v[t], wa0.x, wb0.x, wa0.y, wb0.y, xa[t][0].x, xa[t][0].y);
-        mma16816<T>(acc.v[t], wa0.z, wb0.z, wa0.w, wb0.w, xa[t][0].z, xa[t][0].w);
-        mma16816<T>(acc.v[t], wa1.x, wb1.x, wa1.y, wb1.y, xa[t][1].x, xa[t][1].y);
-        mma16816<T>(acc.v[t], wa1.z, wb1.z, wa1.w, wb1.w, xa[t][1].z, xa[t][1].w);
+      for (int j = 0; j < MAX_BOXES; ++j) {
+        if (j < B) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            mma16816<T>(acc.v[t], wa[j][0].x, wb[j][0].x, wa[j][0].y, wb[j][0].y, xa[j][t][0].x, xa[j][t][0].y);
+            mma16816<T>(acc.v[t], wa[j][0].z, wb[j][0].z, wa[j][0].w, wb[j][0].w, xa[j][t][0].z, xa[j][t][0].w);
+            mma16816<T>(acc.v[t], wa[j][1].x, wb[j][1].x, wa[j][1].y, wb[j][1].y, xa[j][t][1].x, xa[j][t][1].y);
+            mma16816<T>(acc.v[t], wa[j][1].z, wb[j][1].z, wa[j][1].w, wb[j][1].w, xa[j][t][1].z, xa[j][t][1].w);
+          }
+        }
       }
     } else {
-      float wf[2][16];
-      unpack8<T>(wa0, wf[0]);
-      unpack8<T>(wa1, wf[0] + 8);
-      unpack8<T>(wb0, wf[1]);
-      unpack8<T>(wb1, wf[1] + 8);
 #pragma unroll
-      for (int mm = 0; mm < MP; ++mm) {
-        if (mm < a.m) {
-          uint4 x0, x1;
-          if (MODE == MODE_LINEAR) {
-            const unsigned char* xt = xst + static_cast<size_t>(s) * X_STAGE_BYTES;
-            x0 = *reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q));
-            x1 = *reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q + 1));
-          } else {
-            const unsigned char* xt = xs + (ck * a.m + mm) * 128;
-            x0 = *reinterpret_cast<const uint4*>(xt + (((2 * q) ^ (mm & 7)) << 4));
-            x1 = *reinterpret_cast<const uint4*>(xt + (((2 * q + 1) ^ (mm & 7)) << 4));
-          }
-          float xf[16];
-          unpack8<T>(x0, xf);
-          unpack8<T>(x1, xf + 8);
+      for (int j = 0; j < MAX_BOXES; ++j) {
+        if (j < B) {
+          float wf[2][16];
+          unpack8<T>(wa[j][0], wf[0]);
+          unpack8<T>(wa[j][1], wf[0] + 8);
+          unpack8<T>(wb[j][0], wf[1]);
+          unpack8<T>(wb[j][1], wf[1] + 8);
+          const unsigned char* xt = xbox(j);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            sacc[0][mm] = fmaf(wf[0][e], xf[e], sacc[0][mm]);
-            sacc[1][mm] = fmaf(wf[1][e], xf[e], sacc[1][mm]);
+          for (int mm = 0; mm < MP; ++mm) {
+            if (mm < a.m) {
+              float xf[16];
+              unpack8<T>(*reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q)), xf);
+              unpack8<T>(*reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q + 1)), xf + 8);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                sacc[0][mm] = fmaf(wf[0][e], xf[e], sacc[0][mm]);
+                sacc[1][mm] = fmaf(wf[1][e], xf[e], sacc[1][mm]);
+              }
+            }
           }
         }
       }
@@ -655,10 +716,11 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const GenArgs a) {
 // ------------------------------------------------------------ host side
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-int64_t max_grid() { return static_cast<int64_t>(fd_host::sm_count()); }
+constexpr int kMaxCtasPerSm = 2;
+int64_t max_grid() { return static_cast<int64_t>(fd_host::sm_count()) * kMaxCtasPerSm; }
 
 // Workspace layout (fixed for a device, whatever the shape, so one buffer can
-// serve every launch):  [slots: grid x 2 x BR x MT_MAX floats]
+// serve every launch):  [slots: max grid x 2 x BR x MT_MAX floats]
 //                       [counters: kMaxCounters ints][status: 64 ints]
 //                       [MLP intermediate]
 size_t slots_bytes() { return align256(static_cast<size_t>(max_grid()) * 2 * BR * MT_MAX * sizeof(float)); }
@@ -690,46 +752,85 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D map over a [rows, cols] 16-bit matrix with row stride `stride` elements;
-// box = [box_rows x 64 cols], 128B swizzle, out-of-range elements read as 0.
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride, int box_rows) {
+// Tensor map over 16-bit data: `rank` dims (innermost first) with byte strides
+// of the outer dims; boxes of 64 innermost elements, 128B swizzle, elements
+// outside the tensor read as 0.
+bool make_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+              const cuuint32_t* box) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(KC), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, rank, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-size_t tma_smem_bytes(int mode, int mt, int m, int64_t ks, int stages) {
-  const size_t xbytes = mode == MODE_GATEUP ? static_cast<size_t>(ks) * m * 128
-                                            : static_cast<size_t>(stages) * mt * KC * 2;
-  return 1024 + static_cast<size_t>(stages) * W_STAGE_BYTES + ((xbytes + 15) & ~static_cast<size_t>(15)) +
+// [rows, cols] matrix with row stride `stride` elements, boxes of [box_rows x 64].
+bool make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride, int box_rows) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(KC), static_cast<cuuint32_t>(box_rows)};
+  return make_map(map, base, 2, dims, strides, box);
+}
+
+int x_slot_bytes(int m) { return m <= 8 ? 1024 : 2048; }
+
+size_t tma_smem_bytes(int mode, int m, int64_t ks, int stages, int boxes) {
+  const size_t xbytes = mode == MODE_GATEUP ? static_cast<size_t>(ks) * boxes * m * 128
+                                            : static_cast<size_t>(stages) * boxes * x_slot_bytes(m);
+  return 1024 + static_cast<size_t>(stages) * boxes * BOX_BYTES + ((xbytes + 15) & ~static_cast<size_t>(15)) +
          (BR / 2) * MT_MAX * 4 + 2 * MAX_STAGES * 8;
 }
 
-constexpr size_t kSmemLimit = 227 * 1024 - 1024;  // opt-in maximum, less static shared memory
+constexpr size_t kSmemPerSm = 228 * 1024;          // shared memory of one SM
+constexpr size_t kSmemPerCta = 227 * 1024 - 1024;  // opt-in maximum, less static shared memory
 
-// Largest stage count (<= MAX_STAGES) whose shared memory fits; 0 if none >= 2.
-int pick_stages(int mode, int mt, int m, int64_t ks) {
-  for (int s = MAX_STAGES; s >= 2; --s)
-    if (tma_smem_bytes(mode, mt, m, ks, s) <= kSmemLimit) return s;
-  return 0;
+// Pipeline geometry of one launch: CTAs per SM, producer warps, 64-column
+// boxes per step and ring stages.  Measured on B200 over the Llama-3-8B MLP
+// shapes (32-launch CUDA graphs, M = 1 and 8): one CTA per SM with two
+// producer warps, 32 KB steps (two boxes) and four stages streamed fastest
+// (gate/up 5.0 TB/s, down 4.5 TB/s); two CTAs per SM with one producer each
+// were 3-10% slower, 16 KB steps 20-30% slower.
+struct Geometry {
+  int ctas_per_sm, producers, boxes, stages;
+};
+
+Geometry choose_geometry(int mode, int m, int64_t k) {
+  Geometry g{1, 2, 2, 4};
+  if (const char* env = std::getenv("FD_GEMV_GEOMETRY")) {  // tuning override: "cps,producers,boxes,stages"
+    int a = 0, b = 0, c = 0, d = 0;
+    if (std::sscanf(env, "%d,%d,%d,%d", &a, &b, &c, &d) == 4 && a >= 1 && a <= 2 && b >= 1 &&
+        b <= MAX_PRODUCERS && c >= 1 && c <= MAX_BOXES && d >= 2 && d <= MAX_STAGES)
+      g = {a, b, c, d};
+  }
+  const int64_t step_cols = static_cast<int64_t>(g.boxes) * KC;
+  const int64_t ks = (k + step_cols - 1) / step_cols;
+  const size_t per_cta = g.ctas_per_sm == 2 ? kSmemPerSm / 2 - 2048 : kSmemPerCta;
+  while (g.stages > 2 && tma_smem_bytes(mode, m, ks, g.stages, g.boxes) > per_cta) --g.stages;
+  if (tma_smem_bytes(mode, m, ks, g.stages, g.boxes) > per_cta && g.ctas_per_sm == 2) {
+    // Two CTAs do not fit (a wide normalised batch): one CTA, two producers.
+    g.ctas_per_sm = 1;
+    g.producers = std::max(g.producers, 2);
+    g.stages = MAX_STAGES;
+    while (g.stages > 2 && tma_smem_bytes(mode, m, ks, g.stages, g.boxes) > kSmemPerCta) --g.stages;
+  }
+  if (g.ctas_per_sm == 2) g.producers = 1;  // the two-CTA kernels are built for 288 threads
+  g.stages -= g.stages % g.producers;       // every stage is always refilled by the same producer
+  if (g.stages < 2 || tma_smem_bytes(mode, m, ks, g.stages, g.boxes) > kSmemPerCta) g.stages = 0;
+  return g;
 }
 
 template <typename Kern>
-cudaError_t launch_tma(Kern kern, const CUtensorMap& wm, const CUtensorMap& um, const CUtensorMap& xm,
-                       const GemvArgs& a, size_t smem, cudaStream_t st) {
+cudaError_t launch_tma(Kern kern, const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a,
+                       const Geometry& geo, size_t smem, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(max_grid(), a.total));
+  const int64_t grid =
+      std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(fd_host::sm_count()) * geo.ctas_per_sm, a.total));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(CONSUMERS + 32 * geo.producers);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -737,21 +838,38 @@ cudaError_t launch_tma(Kern kern, const CUtensorMap& wm, const CUtensorMap& um, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, wm, um, xm, a);
+  return cudaLaunchKernelEx(&cfg, kern, wm, xm, a);
+}
+
+template <typename T, int MODE, int NT, int KIND, int MP>
+cudaError_t launch_geo(const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, const Geometry& geo,
+                       size_t smem, cudaStream_t st) {
+  if (geo.ctas_per_sm == 2)
+    return launch_tma(gemv_tma_kernel<T, NT, KIND, MP, MODE, CONSUMERS + 32, 2>, wm, xm, a, geo, smem, st);
+  return launch_tma(gemv_tma_kernel<T, NT, KIND, MP, MODE, CONSUMERS + 32 * MAX_PRODUCERS, 1>, wm, xm, a, geo,
+                    smem, st);
 }
 
 template <typename T, int MODE>
-cudaError_t dispatch_tma(const CUtensorMap& wm, const CUtensorMap& um, const CUtensorMap& xm, const GemvArgs& a,
-                         int kind, size_t smem, cudaStream_t st) {
+cudaError_t dispatch_tma(const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, int kind,
+                         const Geometry& geo, size_t smem, cudaStream_t st) {
   if (kind == FD_KIND_DOT) {
-    if (a.m <= 8) return launch_tma(gemv_tma_kernel<T, 1, 0, 1, MODE>, wm, um, xm, a, smem, st);
-    return launch_tma(gemv_tma_kernel<T, 2, 0, 1, MODE>, wm, um, xm, a, smem, st);
+    if (a.m <= 8) return launch_geo<T, MODE, 1, 0, 1>(wm, xm, a, geo, smem, st);
+    return launch_geo<T, MODE, 2, 0, 1>(wm, xm, a, geo, smem, st);
   }
-  if (a.m <= 1) return launch_tma(gemv_tma_kernel<T, 1, 1, 1, MODE>, wm, um, xm, a, smem, st);
-  if (a.m <= 2) return launch_tma(gemv_tma_kernel<T, 1, 1, 2, MODE>, wm, um, xm, a, smem, st);
-  if (a.m <= 4) return launch_tma(gemv_tma_kernel<T, 1, 1, 4, MODE>, wm, um, xm, a, smem, st);
-  if (a.m <= 8) return launch_tma(gemv_tma_kernel<T, 1, 1, 8, MODE>, wm, um, xm, a, smem, st);
-  return launch_tma(gemv_tma_kernel<T, 2, 1, 16, MODE>, wm, um, xm, a, smem, st);
+  // simt: one CTA per SM (its accumulators need the registers)
+  Geometry g1 = geo;
+  if (g1.ctas_per_sm == 2) {
+    g1.ctas_per_sm = 1;
+    g1.producers = 2;
+  }
+  auto L = [&](auto kern) { return launch_tma(kern, wm, xm, a, g1, smem, st); };
+  constexpr int MT1 = CONSUMERS + 32 * MAX_PRODUCERS;
+  if (a.m <= 1) return L(gemv_tma_kernel<T, 1, 1, 1, MODE, MT1, 1>);
+  if (a.m <= 2) return L(gemv_tma_kernel<T, 1, 1, 2, MODE, MT1, 1>);
+  if (a.m <= 4) return L(gemv_tma_kernel<T, 1, 1, 4, MODE, MT1, 1>);
+  if (a.m <= 8) return L(gemv_tma_kernel<T, 1, 1, 8, MODE, MT1, 1>);
+  return L(gemv_tma_kernel<T, 2, 1, 16, MODE, MT1, 1>);
 }
 
 int from_cuda(cudaError_t e) { return e == cudaSuccess ? FD_OK : FD_ERR_LAUNCH; }
@@ -759,21 +877,24 @@ int from_cuda(cudaError_t e) { return e == cudaSuccess ? FD_OK : FD_ERR_LAUNCH; 
 // Launch the stream-K TMA GEMV in LINEAR mode: y = x @ w^T (+bias)(+row_add).
 int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvArgs a, int dtype, int kind,
                   const Workspace& ws, cudaStream_t st) {
-  const int mt = a.m <= 8 ? 8 : 16;
-  a.ks = (a.k + KC - 1) / KC;
+  const Geometry geo = choose_geometry(MODE_LINEAR, a.m, a.k);
+  if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
+  a.boxes = geo.boxes;
+  a.stages = geo.stages;
+  a.ks = (a.k + static_cast<int64_t>(geo.boxes) * KC - 1) / (static_cast<int64_t>(geo.boxes) * KC);
   a.nblocks = (a.n + BR - 1) / BR;
   if (a.nblocks > kMaxCounters) return FD_ERR_UNSUPPORTED;
   a.total = a.nblocks * a.ks;
-  a.stages = pick_stages(MODE_LINEAR, mt, a.m, a.ks);
-  if (a.stages == 0) return FD_ERR_UNSUPPORTED;
+  a.x_slot = x_slot_bytes(a.m);
   a.slots = ws.slots; a.counters = ws.counters; a.status = ws.status;
   CUtensorMap wm, xm;
   // A single row's stride is never used by the TMA unit; keep it legal.
   const int64_t xstride = a.m == 1 ? ((a.k + 7) / 8) * 8 : sxm;
-  if (!make_map(&wm, w, a.n, a.k, swn, BR) || !make_map(&xm, x, a.m, a.k, xstride, mt)) return FD_ERR_LAUNCH;
-  const size_t smem = tma_smem_bytes(MODE_LINEAR, mt, a.m, a.ks, a.stages);
-  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR>(wm, wm, xm, a, kind, smem, st)
-                                   : dispatch_tma<__half, MODE_LINEAR>(wm, wm, xm, a, kind, smem, st);
+  if (!make_map_2d(&wm, w, a.n, a.k, swn, BR) || !make_map_2d(&xm, x, a.m, a.k, xstride, a.m))
+    return FD_ERR_LAUNCH;
+  const size_t smem = tma_smem_bytes(MODE_LINEAR, a.m, a.ks, a.stages, a.boxes);
+  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st)
+                                   : dispatch_tma<__half, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st);
   return from_cuda(e);
 }
 
@@ -787,8 +908,7 @@ int check_mlp_args(const void* hidden, const void* norm_w, int32_t norm_dtype, c
   if (kind != FD_KIND_DOT && kind != FD_KIND_SIMT) return FD_ERR_ARG;
   if (h % 8 || i % 8 || i == 0 || s_gu % 8 || s_gu < h) return FD_ERR_UNSUPPORTED;
   if (!aligned16(hidden) || !aligned16(norm_w) || !aligned16(w_gate_up)) return FD_ERR_UNSUPPORTED;
-  const int64_t ks = (h + KC - 1) / KC;
-  if (m > 0 && pick_stages(MODE_GATEUP, m <= 8 ? 8 : 16, m, ks) == 0) return FD_ERR_UNSUPPORTED;
+  if (m > 0 && choose_geometry(MODE_GATEUP, m, h).stages == 0) return FD_ERR_UNSUPPORTED;
   if ((i + BR / 2 - 1) / (BR / 2) > kMaxCounters) return FD_ERR_UNSUPPORTED;
   return FD_OK;
 }
@@ -797,25 +917,30 @@ int check_mlp_args(const void* hidden, const void* norm_w, int32_t norm_dtype, c
 int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
                    int64_t s_gu, void* mid, int64_t s_mid, int32_t dtype, int32_t m, int64_t h, int64_t i,
                    float eps, int32_t kind, const Workspace& ws, cudaStream_t st) {
+  const Geometry geo = choose_geometry(MODE_GATEUP, m, h);
+  if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
   GemvArgs a = {};
   a.y = static_cast<char*>(mid); a.sym = s_mid; a.syn = 1;
   a.m = m; a.n = 2 * i; a.k = h;
-  a.ks = (h + KC - 1) / KC;
+  a.boxes = geo.boxes;
+  a.stages = geo.stages;
+  a.ks = (h + static_cast<int64_t>(geo.boxes) * KC - 1) / (static_cast<int64_t>(geo.boxes) * KC);
   a.nblocks = (i + BR / 2 - 1) / (BR / 2);
   a.total = a.nblocks * a.ks;
   a.slots = ws.slots; a.counters = ws.counters; a.status = ws.status;
   a.inner = i;
   a.hidden = hidden; a.hidden_stride = h;
   a.norm_w = norm_w; a.norm_dtype = norm_dtype; a.eps = eps;
-  const int mt = m <= 8 ? 8 : 16;
-  a.stages = pick_stages(MODE_GATEUP, mt, m, a.ks);
-  if (a.stages == 0) return FD_ERR_UNSUPPORTED;
-  CUtensorMap gm, um;
-  const char* up = static_cast<const char*>(w_gate_up) + static_cast<int64_t>(i) * s_gu * 2;
-  if (!make_map(&gm, w_gate_up, i, h, s_gu, BR / 2) || !make_map(&um, up, i, h, s_gu, BR / 2)) return FD_ERR_LAUNCH;
-  const size_t smem = tma_smem_bytes(MODE_GATEUP, mt, m, a.ks, a.stages);
-  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, um, gm, a, kind, smem, st)
-                                   : dispatch_tma<__half, MODE_GATEUP>(gm, um, gm, a, kind, smem, st);
+  // 3-D view [2][i][h] of w_gate_up: plane 0 = gate rows, plane 1 = up rows;
+  // one [2 x 64 x 64] box is 64 gate rows over the matching 64 up rows.
+  CUtensorMap gm;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(i), 2};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s_gu) * 2, static_cast<cuuint64_t>(i) * s_gu * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(KC), BR / 2, 2};
+  if (!make_map(&gm, w_gate_up, 3, dims, strides, box)) return FD_ERR_LAUNCH;
+  const size_t smem = tma_smem_bytes(MODE_GATEUP, m, a.ks, a.stages, a.boxes);
+  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st)
+                                   : dispatch_tma<__half, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st);
   return from_cuda(e);
 }
 
@@ -885,7 +1010,7 @@ int fd_mlp_gate_up_out(const void* hidden, const void* norm_w, int32_t norm_dtyp
   const int chk = check_mlp_args(hidden, norm_w, norm_dtype, w_gate_up, s_gu, dtype, m, h, i, kind);
   if (chk != FD_OK) return chk;
   if (m == 0 || h == 0) return FD_OK;
-  if (!mid || !fd_host::aligned16(mid)) return FD_ERR_ARG;
+  if (!mid) return FD_ERR_ARG;
   if (!workspace || workspace_bytes < streamk_ws_bytes()) return FD_ERR_WORKSPACE;
   if (!encode_fn()) return FD_ERR_DEVICE;
   return launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, i, dtype, m, h, i, eps, kind,
@@ -902,7 +1027,7 @@ int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dt
   if (m == 0 || h == 0) return FD_OK;
   if (!w_down || !out) return FD_ERR_ARG;
   if (!(out_dtype == dtype || out_dtype == FD_F32)) return FD_ERR_ARG;
-  if (s_down % 8 || s_down < i || !aligned16(w_down) || !aligned16(out)) return FD_ERR_UNSUPPORTED;
+  if (s_down % 8 || s_down < i || !aligned16(w_down)) return FD_ERR_UNSUPPORTED;
   if (!workspace || workspace_bytes < fd_post_attn_mlp_workspace_bytes(m, h, i)) return FD_ERR_WORKSPACE;
   if (!encode_fn()) return FD_ERR_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
