@@ -49,6 +49,11 @@ def gate_up_launch_bytes(m: int, world: int = 1) -> int:
     return 2 * I * H * 2 // world + m * H * 2 + H * 2 + m * (I // world) * 2
 
 
+def down_launch_bytes(m: int, world: int = 1) -> int:
+    """Algorithmic bytes of one down-kernel launch: weight, mid, residual, output."""
+    return H * I * 2 // world + m * (I // world) * 2 + 2 * m * H * 2
+
+
 def peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -330,7 +335,40 @@ def run_ours(args) -> None:
     us8 = ms8 * 1e3 / LAYERS
     bytes8 = layer_bytes(8, world=world)
 
-    # ---- dominant kernel alone: the gate/up kernel, 32 launches per graph
+    # ---- the same stack as one launch per layer (the per-call public API)
+    per_layer_us = None
+    if world == 1:
+        stack_pl = MlpStack(layers, args.m, EPS, kind="dot", fused=False)
+        ms_pl, _ = time_stack(stack_pl, max(3, args.steps // 5), args.warmup)
+        per_layer_us = ms_pl * 1e3 / LAYERS
+        del stack_pl
+
+    # ---- the same stack as two stream-K kernels per layer (gate/up, then down + residual)
+    two_kernel_us = None
+    if world == 1:
+        hb = [torch.zeros(args.m, H, device=device, dtype=torch.bfloat16) for _ in range(3)]
+        mid2 = torch.empty(args.m, I, device=device, dtype=torch.bfloat16)
+
+        def two_kernel_all():
+            x = hb[0]
+            for li, (nw, wgu, wd) in enumerate(layers):
+                K.mlp_gate_up_out(x, nw, wgu, mid2, EPS, "dot")
+                y = hb[1 + (li & 1)]
+                K.linear_out(mid2, wd, y, row_add=x, kind="dot")
+                x = y
+
+        two_kernel_all()
+        t_stream = torch.cuda.Stream()
+        t_stream.wait_stream(torch.cuda.current_stream())
+        graph_tk = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_tk, stream=t_stream):
+            two_kernel_all()
+        for _ in range(args.warmup):
+            graph_tk.replay()
+        two_kernel_us = cuda_time(torch, graph_tk.replay, max(3, args.steps // 5)) * 1e3 / LAYERS
+        del graph_tk
+
+    # ---- the gate/up stage alone (its own kernel), 32 launches per graph
     mid = torch.empty(args.m, I // world, device=device, dtype=torch.bfloat16)
     xk = torch.randn(args.m, H, device=device, dtype=torch.bfloat16)
 
@@ -349,9 +387,29 @@ def run_ours(args) -> None:
         gate_up_all()
     for _ in range(args.warmup):
         graph_gu.replay()
-    ms_gu = max_over_ranks(cuda_time(torch, graph_gu.replay, args.steps)) / LAYERS
+    ms_gu = max_over_ranks(cuda_time(torch, graph_gu.replay, max(3, args.steps // 5))) / LAYERS
     gu_bytes = gate_up_launch_bytes(args.m, world)
     gu_gbs = gu_bytes / (ms_gu * 1e-3) / 1e9
+
+    # ---- the down stage alone (+ residual), 32 launches per graph
+    yd = torch.empty(args.m, H, device=device, dtype=torch.bfloat16)
+    mid_d = torch.randn(args.m, I // world, device=device, dtype=torch.bfloat16)
+
+    def down_all():
+        for _, _, wd in layers:
+            K.linear_out(mid_d, wd, yd, row_add=xk, kind="dot")
+
+    down_all()
+    d_stream = torch.cuda.Stream()
+    d_stream.wait_stream(torch.cuda.current_stream())
+    graph_dn = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_dn, stream=d_stream):
+        down_all()
+    for _ in range(args.warmup):
+        graph_dn.replay()
+    ms_dn = max_over_ranks(cuda_time(torch, graph_dn.replay, max(3, args.steps // 5))) / LAYERS
+    dn_bytes = down_launch_bytes(args.m, world)
+    dn_gbs = dn_bytes / (ms_dn * 1e-3) / 1e9
 
     # ---- e2e: public API with host buffers, every step H2D + 32 layers + D2H
     host_in = torch.randn(args.m, H, dtype=torch.bfloat16).pin_memory()
@@ -394,7 +452,7 @@ def run_ours(args) -> None:
                          f"(numpy fp32 oracle port of reference.py:66-79), ~{args.cpu_seconds:.0f} s"}
 
     if rank == 0:
-        traffic = committed_traffic().get("gate_up_kernel_bytes_per_launch")
+        traffic = committed_traffic().get(f"gate_up_kernel_bytes_per_launch_m{args.m}") if world == 1 else None
         gbs1 = bytes1 / (us1 * 1e-6) / 1e9
         line = {
             "metric": METRIC,
@@ -421,11 +479,22 @@ def run_ours(args) -> None:
             "copy_roof_gbs": roof,
             "m8": {"us_per_layer": us8, "ms_per_step": ms8, "hbm_gbs": bytes8 / (us8 * 1e-6) / 1e9,
                    "hbm_frac": bytes8 / (us8 * 1e-6) / 1e9 / pk["hbm_gbs"]},
+            # the dominant kernel: RMSNorm + gate/up GEMV + SwiGLU (2/3 of a layer's bytes)
             "roofline": {
-                "kernel": "gemv_streamk_kernel gate/up mode (RMSNorm + gate/up GEMV + SwiGLU)",
+                "kernel": "gemv_tma_kernel<bf16, GATEUP> (RMSNorm prologue + gate/up GEMV + SwiGLU epilogue)",
                 "bound": "hbm", "achieved": gu_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": gu_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
                 "traffic": traffic, "bytes_per_launch": gu_bytes, "us_per_launch": ms_gu * 1e3,
+                "timed": "32 launches (one per layer's weights) in one CUDA graph, CUDA events",
+            },
+            "kernels": {
+                "gate_up_stage_alone": {"us": ms_gu * 1e3, "gbs": gu_gbs, "bytes": gu_bytes,
+                                        "frac": gu_gbs / pk["hbm_gbs"]},
+                "down_stage_alone": {"us": ms_dn * 1e3, "gbs": dn_gbs, "bytes": dn_bytes,
+                                     "frac": dn_gbs / pk["hbm_gbs"]},
+                "layer": {"us": us1, "gbs": gbs1, "bytes": bytes1, "frac": gbs1 / pk["hbm_gbs"]},
+                "per_layer_calls_us_per_layer": per_layer_us,
+                "two_kernel_us_per_layer": two_kernel_us,
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_s * 1e6 / LAYERS, "unit": "us/layer",
@@ -433,13 +502,14 @@ def run_ours(args) -> None:
                     "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
                     "api": "fused_decode_b200.stack.MlpStack (pinned host in, graph replay, pinned host out)",
                     "eager_api_us_per_layer": e2e_eager_s * 1e6 / LAYERS},
-            # per layer: gate/up kernel + down kernel (+ residual-add kernel under TP)
-            "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 3),
+            # single GPU: two launches per layer; tensor-parallel: gate/up, down
+            # (fp32 partial) and residual-add launches per layer (+ NCCL)
+            "gpu_launches": args.steps * (stack1.launches_per_replay if world == 1 else 3 * LAYERS),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        del stack1, stack8, graph_gu
+        del stack1, stack8, graph_gu, graph_dn
         torch.cuda.synchronize()
         dist.destroy_process_group()
 

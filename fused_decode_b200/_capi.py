@@ -93,6 +93,17 @@ SIGNATURES: dict[str, tuple] = {
             c_vp, c_size, c_vp,          # workspace, bytes, stream
         ],
     ),
+    "fd_post_attn_mlp_stack_out": (
+        c_i32,
+        [
+            c_vp, c_i32,                 # hidden, layers
+            c_vp, c_i32,                 # norm_w[], norm_dtype
+            c_vp, c_i64, c_vp, c_i64,    # w_gate_up[], s_gu, w_down[], s_down
+            c_vp, c_i32, c_i32,          # out, dtype, m
+            c_i64, c_i64, c_f32, c_i32,  # h, i, eps, kind
+            c_vp, c_size, c_vp,          # workspace, bytes, stream
+        ],
+    ),
     "fd_residual_add_out": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i64, c_vp]),
     "fd_copy": (c_i32, [c_vp, c_vp, c_size, c_vp]),
     "fd_triad": (c_i32, [c_vp, c_vp, c_vp, c_i64, c_i32, c_f32, c_vp]),
@@ -140,6 +151,11 @@ def check(status: int, what: str) -> None:
 
 def stream_of(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def ptr_array(ptrs) -> ctypes.Array:
+    """A host array of device pointers (``const void* const*``)."""
+    return (c_vp * len(ptrs))(*ptrs)
 
 
 def rows(layout) -> FdRows:

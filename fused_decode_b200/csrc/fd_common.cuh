@@ -84,6 +84,15 @@ FD_DEV float load_as_f32(const void* p, int dtype, int64_t i) {
   return __half2float(static_cast<const __half*>(p)[i]);
 }
 
+// As load_as_f32, but read through L2 only: for data another CTA may have
+// written earlier in the same kernel.
+FD_DEV float load_as_f32_cg(const void* p, int dtype, int64_t i) {
+  if (dtype == FD_F32) return __ldcg(static_cast<const float*>(p) + i);
+  const unsigned short bits = __ldcg(static_cast<const unsigned short*>(p) + i);
+  if (dtype == FD_BF16) return __bfloat162float(__ushort_as_bfloat16(bits));
+  return __half2float(__ushort_as_half(bits));
+}
+
 // 8 consecutive elements of a runtime-typed array as fp32 (16-byte aligned for
 // 16-bit types, 32-byte region for f32 -- two 16-byte loads).
 FD_DEV void load8_as_f32(const void* p, int dtype, float* f) {

@@ -1,0 +1,870 @@
+// The weight-streaming engine of the decode GEMV kernels (fd_gemv.cu): a plain
+// linear and the MLP's gate/up stage run the same producer/consumer phases.
+//
+//  * Stream-K over a weight.  The weight is cut into blocks of 128 rows; a
+//    block is a run of KS steps of B x 64 columns.  Every CTA of the grid owns
+//    an equal contiguous piece of the flat step range [0, nblocks*KS), so
+//    every SM streams the same number of weight bytes whatever N and K are.
+//  * TMA ring.  P producer warps take turns issuing each step's B 2-D/3-D
+//    tensor-map loads (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//    of a [128 x 64] weight box -- and, for a plain GEMV, the [M x 64]
+//    activation boxes -- into an S-stage shared-memory ring guarded by
+//    mbarriers (full: data landed, empty: all consumer warps read it).
+//    Measured on B200: one issuing thread keeps only about two stages in
+//    flight, so two producer warps with 32 KB steps are what saturate HBM.
+//  * Eight consumer warps own 16 weight rows each.  "dot" kind: each lane
+//    reads 16 contiguous columns of its two rows (rows g and g+8, g = lane/4,
+//    q = lane%4) -- conflict-free under the 128B swizzle -- and feeds four
+//    mma.sync m16n8k16 per box (swap-AB: weight = A, batch = N of 8 or 16).
+//    The physical columns a lane holds map to logical MMA k-indices by one
+//    fixed permutation applied to both A and B, so the sum is exact.  "simt"
+//    kind: the same tiles, fp32 FMAs against all M rows.
+//  * Split-K partials go to per-CTA slots in a caller workspace; the last CTA
+//    to finish a block (an atomic counter) sums the slots in CTA order --
+//    deterministic, no inter-CTA waiting -- applies the epilogue and re-zeroes
+//    the counter, so the workspace is ready for the next launch or replay.
+//  * Every wait is bounded (globaltimer): on expiry the CTA sets a bit in the
+//    workspace status word and leaves instead of hanging.
+#pragma once
+
+#include "fd_common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+
+namespace fd_stream {
+
+using namespace fd;
+
+constexpr int GW = 8;                      // consumer warps per CTA
+constexpr int BR = GW * 16;                // weight rows per block
+constexpr int KC = 64;                     // columns per box (128 bytes of a 16-bit row)
+constexpr int BOX_BYTES = BR * KC * 2;     // 16 KB weight box
+constexpr int MAX_BOXES = 2;               // boxes per step
+constexpr int MT_MAX = 16;                 // max batch rows
+constexpr int CONSUMERS = GW * 32;
+constexpr int MAX_PRODUCERS = 3;
+constexpr int MAX_STAGES = 12;
+constexpr int64_t kMaxCounters = 1 << 16;  // blocks per launch (N <= 8M rows)
+constexpr uint64_t kWaitNs = 2000000000ull;      // bounded mbarrier waits: 2 s
+
+// Status bits written to the workspace status word.
+constexpr int kStatusFullTimeout = 1;
+constexpr int kStatusEmptyTimeout = 2;
+
+enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1 };
+
+// One phase of streaming: a GEMV (LINEAR) or the MLP gate/up stage (GATEUP).
+struct GemvArgs {
+  const void* bias;
+  int32_t bias_dtype;
+  int64_t sbias;
+  const void* ra;
+  int32_t ra_dtype;
+  int64_t srm, srn;
+  char* y;
+  int64_t sym, syn;
+  int32_t y_f32;    // LINEAR mode: store fp32 instead of T (tensor-parallel partials)
+  int32_t m;
+  int64_t n, k;
+  // stream-K geometry
+  int64_t ks;       // steps per block
+  int64_t nblocks;
+  int64_t total;    // nblocks * ks
+  int32_t stages;   // S
+  int32_t boxes;    // B: 64-column boxes per step
+  int32_t x_slot;   // LINEAR: bytes per activation box slot (1024-aligned)
+  float* slots;     // [grid][2][BR * MT_MAX]
+  int* counters;    // [nblocks]
+  int* status;      // error bits
+  // gate/up mode
+  int64_t inner;            // I: number of gate (= up) rows
+  const void* hidden;       // [m, k] rows, row stride hidden_stride
+  int64_t hidden_stride;
+  const void* norm_w;
+  int32_t norm_dtype;
+  float eps;
+};
+
+// ------------------------------------------------------------ PTX helpers
+template <typename T>
+FD_DEV void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1);
+template <>
+FD_DEV void mma16816<__nv_bfloat16>(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                    uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <>
+FD_DEV void mma16816<__half>(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+FD_DEV uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+FD_DEV uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+FD_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+FD_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+FD_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+FD_DEV uint32_t mbar_try(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.b32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok;
+}
+// Wait for the phase with the given parity to complete; false after kWaitNs.
+FD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  if (mbar_try(addr, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try(addr, parity)) return true;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+FD_DEV uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// 2-D / 3-D tiled TMA loads into this CTA's shared memory, completing on `bar`
+// (no multicast: every CTA fetches its own tiles).
+FD_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+FD_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z, uint64_t* bar,
+                        uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+FD_DEV void tma_load_2d_plain(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+FD_DEV void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+FD_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS) : "memory"); }
+FD_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+FD_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk c of row r inside a 128B-swizzled tile whose
+// rows are 128 bytes (TMA CU_TENSOR_MAP_SWIZZLE_128B, 1024-byte aligned base).
+FD_DEV uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// ------------------------------------------------------------ stream-K split
+FD_DEV int64_t range_start(int64_t c, int64_t total, int64_t G) { return c * total / G; }
+// The CTA whose range holds step t.
+FD_DEV int64_t cta_of(int64_t t, int64_t total, int64_t G) { return ((t + 1) * G - 1) / total; }
+
+FD_DEV float silu_mul(float g, float u) {
+  // Stable sigmoid, as the reference kernel computes it (kernels.py:448-451).
+  const float e = expf(-fabsf(g));
+  const float sig = g >= 0.f ? 1.0f / (1.0f + e) : e / (1.0f + e);
+  return g * sig * u;
+}
+
+// Accumulator ownership shared by both kinds: lane (g, q) owns, for tile t and
+// element e, weight row g + 8*(e>>1) of its warp and batch column
+// 8t + 2q + (e&1) -- the m16n8 C-fragment layout.
+template <int NT>
+struct Acc {
+  float v[NT][4];
+  FD_DEV void zero() {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[t][e] = 0.f;
+  }
+};
+
+// ------------------------------------------------------------ epilogues
+template <typename T, int NT, int MODE>
+struct Epilogue;
+
+// Plain linear: y = round(acc + bias + row_add)  (or the fp32 sum).
+template <typename T, int NT>
+struct Epilogue<T, NT, MODE_LINEAR> {
+  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* /*xchg*/) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
+        const int col = 8 * t + 2 * q + (e & 1);
+        if (row < a.n && col < a.m) {
+          float v = acc.v[t][e];
+          if (a.bias) v += load_as_f32(a.bias, a.bias_dtype, row * a.sbias);
+          // row_add may have been written earlier in this kernel by another CTA: read through L2
+          if (a.ra) v += load_as_f32_cg(a.ra, a.ra_dtype, col * a.srm + row * a.srn);
+          if (a.y_f32)
+            reinterpret_cast<float*>(a.y)[col * a.sym + row * a.syn] = v;
+          else
+            reinterpret_cast<T*>(a.y)[col * a.sym + row * a.syn] = from_f32<T>(v);
+        }
+      }
+    }
+  }
+};
+
+// Gate/up + SwiGLU: warps 0..3 hold gate rows, warps 4..7 the matching up rows.
+// gate and up are rounded to T first, as the reference rounds gate_up
+// (reference.py:390, ops.py:313), then mid = round(silu(gate) * up).
+template <typename T, int NT>
+struct Epilogue<T, NT, MODE_GATEUP> {
+  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* xchg) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    constexpr int HALF = GW / 2;
+    if (warp >= HALF) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = 16 * (warp - HALF) + g + 8 * (e >> 1);
+          const int col = 8 * t + 2 * q + (e & 1);
+          xchg[r * MT_MAX + col] = acc.v[t][e];
+        }
+    }
+    consumer_sync();
+    if (warp < HALF) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = 16 * warp + g + 8 * (e >> 1);
+          const int col = 8 * t + 2 * q + (e & 1);
+          const int64_t j = blk * (BR / 2) + r;
+          if (j < a.inner && col < a.m) {
+            const float gt = round_to<T>(acc.v[t][e]);
+            const float up = round_to<T>(xchg[r * MT_MAX + col]);
+            reinterpret_cast<T*>(a.y)[col * a.sym + j] = from_f32<T>(silu_mul(gt, up));
+          }
+        }
+    }
+    consumer_sync();
+  }
+};
+
+// Block `blk` ends inside this CTA's range [s0, s1): finish it directly if the
+// CTA covered all of it, else publish the partial and let the last of the
+// block's CTAs reduce.  Called by all consumer threads together.
+template <typename T, int NT, int MODE>
+FD_DEV void flush_block(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* xchg, int64_t s0, int64_t s1,
+                        int64_t G, int64_t c, int* s_last) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const bool covered = (s0 <= blk * a.ks) && (s1 >= (blk + 1) * a.ks);
+  if (covered) {
+    Epilogue<T, NT, MODE>::run(a, blk, acc, xchg);
+    return;
+  }
+  const int slot = (blk == s0 / a.ks) ? 0 : 1;
+  float* sp = a.slots + (c * 2 + slot) * (BR * MT_MAX);
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 16 * warp + g + 8 * h;
+      const int col = 8 * t + 2 * q;
+      *reinterpret_cast<float2*>(sp + r * MT_MAX + col) = make_float2(acc.v[t][2 * h], acc.v[t][2 * h + 1]);
+    }
+  __threadfence();
+  consumer_sync();
+  const int64_t cf = cta_of(blk * a.ks, a.total, G);
+  const int64_t cl = cta_of((blk + 1) * a.ks - 1, a.total, G);
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(a.counters + blk, 1);
+    *s_last = (old == static_cast<int>(cl - cf));
+  }
+  consumer_sync();
+  if (*s_last) {
+    __threadfence();
+    Acc<NT> sum;
+    sum.zero();
+    // Contributors' slots are loaded UNROLL at a time, all in flight together
+    // (one L2 round trip per batch under full HBM load, not one per slot), then
+    // added in CTA order so the result does not depend on timing.
+    constexpr int UNROLL = 4;
+    for (int64_t c0 = cf; c0 <= cl; c0 += UNROLL) {
+      float2 v[UNROLL][NT][2];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int64_t cc = c0 + u;
+        const int sl = (cc <= cl && blk != range_start(cc, a.total, G) / a.ks) ? 1 : 0;
+        const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            v[u][t][h] = cc <= cl ? __ldcg(reinterpret_cast<const float2*>(rp + (16 * warp + g + 8 * h) * MT_MAX +
+                                                                           8 * t + 2 * q))
+                                  : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            sum.v[t][2 * h] += v[u][t][h].x;
+            sum.v[t][2 * h + 1] += v[u][t][h].y;
+          }
+    }
+    Epilogue<T, NT, MODE>::run(a, blk, sum, xchg);
+    if (threadIdx.x == 0) a.counters[blk] = 0;
+  }
+}
+
+// ------------------------------------------------------------ the ring
+// Shared-memory layout (1024-byte aligned base):
+//   [W ring: S x B x 16 KB][X region][xchg: 64 x 16 floats][full[12]][empty[12]]
+// X region: LINEAR activation boxes (S x B x x_slot), or the GATEUP normalised
+// batch (ks x B chunks of [m x 128 B]).
+struct Ring {
+  unsigned char* wst;
+  unsigned char* xreg;
+  float* xchg;
+  uint64_t* full;
+  uint64_t* empty;
+  int S, B, x_slot;
+  int64_t w_stage;
+};
+
+FD_DEV Ring carve_ring(unsigned char* smem_raw, int S, int B, int x_slot, int64_t x_bytes) {
+  Ring r;
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~static_cast<uintptr_t>(1023));
+  r.S = S;
+  r.B = B;
+  r.x_slot = x_slot;
+  r.w_stage = static_cast<int64_t>(B) * BOX_BYTES;
+  r.wst = smem;
+  r.xreg = smem + S * r.w_stage;
+  r.xchg = reinterpret_cast<float*>(r.xreg + ((x_bytes + 15) & ~15ll));
+  r.full = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(r.xchg) + (BR / 2) * MT_MAX * 4);
+  r.empty = r.full + MAX_STAGES;
+  return r;
+}
+
+FD_DEV void ring_init(const Ring& r) {
+  for (int i = 0; i < r.S; ++i) {
+    mbar_init(&r.full[i], 1);
+    mbar_init(&r.empty[i], GW);
+  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+template <int MODE>
+FD_DEV uint32_t stage_bytes(const Ring& r, const GemvArgs& a) {
+  return static_cast<uint32_t>(r.w_stage) + (MODE == MODE_LINEAR ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
+}
+
+// Weight boxes of phase step t into ring index gi.
+template <int MODE>
+FD_DEV void issue_w(const Ring& r, const CUtensorMap* map, const GemvArgs& a, int64_t t, int64_t gi, uint64_t pol) {
+  const int64_t b = t / a.ks, kk = t - b * a.ks;
+  const int s = static_cast<int>(gi % r.S);
+  unsigned char* dst = r.wst + s * r.w_stage;
+  for (int j = 0; j < r.B; ++j) {
+    const int32_t col = static_cast<int32_t>((kk * r.B + j) * KC);
+    if (MODE == MODE_GATEUP)
+      tma_load_3d(dst + j * BOX_BYTES, map, col, static_cast<int32_t>(b * (BR / 2)), 0, &r.full[s], pol);
+    else
+      tma_load_2d(dst + j * BOX_BYTES, map, col, static_cast<int32_t>(b * BR), &r.full[s], pol);
+  }
+}
+// Activation boxes (LINEAR) of phase step t into ring index gi.
+FD_DEV void issue_x(const Ring& r, const CUtensorMap* xmap, const GemvArgs& a, int64_t t, int64_t gi) {
+  const int64_t kk = t - (t / a.ks) * a.ks;
+  const int s = static_cast<int>(gi % r.S);
+  for (int j = 0; j < r.B; ++j)
+    tma_load_2d_plain(r.xreg + (s * r.B + j) * r.x_slot, xmap, static_cast<int32_t>((kk * r.B + j) * KC), 0,
+                      &r.full[s]);
+}
+
+// Producer p's share of one phase: phase steps [s0, s1) occupy ring indices
+// base .. base + (s1 - s0).  For a LINEAR phase the activation may be written
+// by whatever ran before: the weight boxes of the phase's first S steps go out
+// first, then `ready()` (a bounded wait) makes the activation readable, then
+// their activation boxes follow.  Returns false when a wait expired.
+template <int MODE, typename Ready>
+FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensorMap* xmap, const GemvArgs& a,
+                          int64_t s0, int64_t s1, int64_t base, int p, int P, uint64_t pol, int* s_abort,
+                          Ready ready) {
+  const int64_t n = s1 - s0;
+  const uint32_t sb = stage_bytes<MODE>(r, a);
+  const int64_t npre = n < r.S ? n : r.S;
+  // first index of this producer at or after `base`
+  int64_t first = base + ((p - base % P) % P + P) % P;
+  auto acquire = [&](int64_t gi) -> bool {  // stage of ring index gi is free again
+    if (gi < r.S) return true;
+    const int s = static_cast<int>(gi % r.S);
+    if (!mbar_wait(&r.empty[s], static_cast<uint32_t>((gi / r.S - 1) & 1))) {
+      atomicOr(a.status, kStatusEmptyTimeout);
+      *s_abort = 1;
+      return false;
+    }
+    return !*reinterpret_cast<volatile int*>(s_abort);
+  };
+  int64_t gi = first;
+  for (; gi < base + npre; gi += P) {
+    if (!acquire(gi)) return false;
+    mbar_expect_tx(&r.full[gi % r.S], sb);
+    issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
+  }
+  if (MODE == MODE_LINEAR) {
+    if (!ready()) return false;
+    for (int64_t g2 = first; g2 < base + npre; g2 += P) issue_x(r, xmap, a, s0 + (g2 - base), g2);
+  }
+  for (; gi < base + n; gi += P) {
+    if (!acquire(gi)) return false;
+    mbar_expect_tx(&r.full[gi % r.S], sb);
+    issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
+    if (MODE == MODE_LINEAR) issue_x(r, xmap, a, s0 + (gi - base), gi);
+  }
+  return true;
+}
+
+// Producer p: wait until every copy it issued to the last S ring indices
+// [end - S, end) has landed (their stages are never refilled, so the phase
+// parity is unambiguous).  Keeps the CTA alive while copies are in flight.
+FD_DEV void producer_drain(const Ring& r, int64_t end, int p, int P) {
+  const int64_t lo = end > r.S ? end - r.S : 0;
+  for (int64_t gi = lo + ((p - lo % P) % P + P) % P; gi < end; gi += P)
+    if (!mbar_wait(&r.full[gi % r.S], static_cast<uint32_t>((gi / r.S) & 1))) break;
+}
+
+// RMSNorm of the m hidden rows into the GATEUP X region, rounded to T
+// (reference.py:389 rounds `normed` to the activation dtype), stored as
+// 64-column chunks of [m x 128 B] with the same swizzle as a TMA tile;
+// columns past k (to the end of the last step) are zero.  The hidden rows are
+// read through L2 (they may have been written earlier in this kernel).  Under
+// full HBM load an L2 round trip costs microseconds, so rows are processed in
+// groups whose loads (hidden and norm weight) are all issued at once: one
+// round trip per group -- a single group for m * k <= 8 * 256 * 8 (k <= 8192
+// here; wider rows take two passes).
+// Called by all consumer threads; ends with a consumer barrier.
+template <typename T>
+FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]) {
+  constexpr int REGS = 8;  // 16-byte vectors of hidden held per thread per group
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  unsigned char* xs = r.xreg;
+  const int nvec = static_cast<int>(a.k / 8);
+  const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
+  const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;  // vectors per thread per row
+  const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
+  if (jv <= 4) {
+    const int rows_per_group = REGS / jv;
+    for (int r0 = 0; r0 < a.m; r0 += rows_per_group) {
+      const int nr = min(rows_per_group, a.m - r0);
+      uint4 hv[REGS];
+      float wv[4][8];
+      // issue every load of the group first
+#pragma unroll
+      for (int e = 0; e < REGS; ++e) {
+        const int rr = e / jv, j = e - (e / jv) * jv;
+        const int v = tid + j * CONSUMERS;
+        hv[e] = make_uint4(0, 0, 0, 0);
+        if (rr < nr && v < nvec)
+          hv[e] = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) +
+                                                         (r0 + rr) * a.hidden_stride) + v);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int v = tid + j * CONSUMERS;
+        if (j < jv && v < nvec)
+          load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv[j]);
+      }
+      float ss[REGS];
+#pragma unroll
+      for (int e = 0; e < REGS; ++e) {
+        float f[8];
+        unpack8<T>(hv[e], f);
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t += f[q] * f[q];
+        ss[e] = t;
+      }
+      // per-row partial sums -> warp -> shared
+#pragma unroll
+      for (int rr = 0; rr < REGS; ++rr) {
+        if (rr < nr) {
+          float t = 0.f;
+#pragma unroll
+          for (int e = 0; e < REGS; ++e)
+            if (e / jv == rr) t += ss[e];
+          t = warp_sum(t);
+          if (lane == 0) s_sumsq[warp][rr] = t;
+        }
+      }
+      consumer_sync();
+#pragma unroll
+      for (int e = 0; e < REGS; ++e) {
+        const int rr = e / jv, j = e - (e / jv) * jv;
+        const int v = tid + j * CONSUMERS;
+        if (rr < nr && v < nvec_pad) {
+          float tot = 0.f;
+#pragma unroll
+          for (int w = 0; w < GW; ++w) tot += s_sumsq[w][rr];
+          const float inv = 1.0f / sqrtf(tot / static_cast<float>(a.k) + a.eps);
+          uint4 packed = make_uint4(0, 0, 0, 0);
+          if (v < nvec) {
+            float f[8], o[8];
+            unpack8<T>(hv[e], f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float w = j == 0 ? wv[0][q] : j == 1 ? wv[1][q] : j == 2 ? wv[2][q] : wv[3][q];
+              o[q] = f[q] * inv * w;
+            }
+            packed = pack8<T>(o);
+          }
+          const int mrow = r0 + rr, chunk = v >> 3, cc = v & 7;
+          *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 +
+                                    ((cc ^ (mrow & 7)) << 4)) = packed;
+        }
+      }
+      consumer_sync();  // s_sumsq is reused by the next group
+    }
+    return;
+  }
+  // Very wide rows: two passes per row, loads of a pass in flight together.
+  for (int mrow = 0; mrow < a.m; ++mrow) {
+    const uint4* hr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride);
+    float ss = 0.f;
+    for (int v = tid; v < nvec; v += CONSUMERS) {
+      float f[8];
+      unpack8<T>(__ldcg(hr + v), f);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss += f[q] * f[q];
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) s_sumsq[warp][0] = ss;
+    consumer_sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < GW; ++w) tot += s_sumsq[w][0];
+    const float inv = 1.0f / sqrtf(tot / static_cast<float>(a.k) + a.eps);
+    for (int v = tid; v < nvec_pad; v += CONSUMERS) {
+      uint4 packed = make_uint4(0, 0, 0, 0);
+      if (v < nvec) {
+        float f[8], wv[8], o[8];
+        unpack8<T>(__ldcg(hr + v), f);
+        load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = f[q] * inv * wv[q];
+        packed = pack8<T>(o);
+      }
+      const int chunk = v >> 3, cc = v & 7;
+      *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4)) =
+          packed;
+    }
+    consumer_sync();
+  }
+}
+
+// Consumer warps' share of one phase: phase steps [s0, s1) at ring indices
+// base ..; flushes every finished block.  Returns false when a wait expired.
+template <typename T, int NT, int KIND, int MP, int MODE>
+FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t s1, int64_t base, int64_t G,
+                          int64_t c, int* s_last, int* s_abort) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int B = r.B;
+  Acc<NT> acc;
+  acc.zero();
+  float sacc[2][MP];
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+    for (int mm = 0; mm < MP; ++mm) sacc[rr][mm] = 0.f;
+
+  const int r0 = 16 * warp + g;  // weight rows of this lane in every box: r0, r0 + 8
+  int64_t cb = s0 / a.ks, ck = s0 - (s0 / a.ks) * a.ks;
+  for (int64_t it = 0; it < s1 - s0; ++it) {
+    const int64_t gi = base + it;
+    const int s = static_cast<int>(gi % r.S);
+    if (!mbar_wait(&r.full[s], static_cast<uint32_t>((gi / r.S) & 1))) {
+      atomicOr(a.status, kStatusFullTimeout);
+      *s_abort = 1;
+      return false;  // every consumer warp times out on this same stage
+    }
+    uint4 wa[MAX_BOXES][2], wb[MAX_BOXES][2];
+#pragma unroll
+    for (int j = 0; j < MAX_BOXES; ++j) {
+      if (j < B) {
+        const unsigned char* wt = r.wst + s * r.w_stage + j * BOX_BYTES;
+        wa[j][0] = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q));
+        wa[j][1] = *reinterpret_cast<const uint4*>(wt + swz(r0, 2 * q + 1));
+        wb[j][0] = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q));
+        wb[j][1] = *reinterpret_cast<const uint4*>(wt + swz(r0 + 8, 2 * q + 1));
+      }
+    }
+    // activation box j of this step: [m rows x 128 B] (swizzled by row & 7)
+    auto xbox = [&](int j) -> const unsigned char* {
+      return MODE == MODE_LINEAR ? r.xreg + (s * B + j) * r.x_slot : r.xreg + ((ck * B + j) * a.m) * 128;
+    };
+    if (KIND == 0) {
+      uint4 xa[MAX_BOXES][NT][2];
+#pragma unroll
+      for (int j = 0; j < MAX_BOXES; ++j) {
+        if (j < B) {
+          const unsigned char* xt = xbox(j);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const int n = g + 8 * t;
+            if (n < a.m) {
+              xa[j][t][0] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q));
+              xa[j][t][1] = *reinterpret_cast<const uint4*>(xt + swz(n, 2 * q + 1));
+            } else {
+              xa[j][t][0] = make_uint4(0, 0, 0, 0);
+              xa[j][t][1] = make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&r.empty[s]);
+      // physical column 16q + 4h + j  <->  logical k of MMA h: (2q, 2q+1, 2q+8, 2q+9)
+#pragma unroll
+      for (int j = 0; j < MAX_BOXES; ++j) {
+        if (j < B) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            mma16816<T>(acc.v[t], wa[j][0].x, wb[j][0].x, wa[j][0].y, wb[j][0].y, xa[j][t][0].x, xa[j][t][0].y);
+            mma16816<T>(acc.v[t], wa[j][0].z, wb[j][0].z, wa[j][0].w, wb[j][0].w, xa[j][t][0].z, xa[j][t][0].w);
+            mma16816<T>(acc.v[t], wa[j][1].x, wb[j][1].x, wa[j][1].y, wb[j][1].y, xa[j][t][1].x, xa[j][t][1].y);
+            mma16816<T>(acc.v[t], wa[j][1].z, wb[j][1].z, wa[j][1].w, wb[j][1].w, xa[j][t][1].z, xa[j][t][1].w);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < MAX_BOXES; ++j) {
+        if (j < B) {
+          float wf[2][16];
+          unpack8<T>(wa[j][0], wf[0]);
+          unpack8<T>(wa[j][1], wf[0] + 8);
+          unpack8<T>(wb[j][0], wf[1]);
+          unpack8<T>(wb[j][1], wf[1] + 8);
+          const unsigned char* xt = xbox(j);
+#pragma unroll
+          for (int mm = 0; mm < MP; ++mm) {
+            if (mm < a.m) {
+              float xf[16];
+              unpack8<T>(*reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q)), xf);
+              unpack8<T>(*reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q + 1)), xf + 8);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                sacc[0][mm] = fmaf(wf[0][e], xf[e], sacc[0][mm]);
+                sacc[1][mm] = fmaf(wf[1][e], xf[e], sacc[1][mm]);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&r.empty[s]);
+    }
+    // ---- block finished (or range ends): flush
+    ++ck;
+    if (ck == a.ks || it + 1 == s1 - s0) {
+      if (KIND == 1) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+          for (int mm = 0; mm < MP; ++mm) {
+            float v = sacc[rr][mm];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            sacc[rr][mm] = v;
+          }
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float v = 0.f;
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const int col = 8 * t + 2 * qq + (e & 1);
+              if (col < MP && qq == q) v = sacc[e >> 1][col];
+            }
+            acc.v[t][e] = v;
+          }
+      }
+      flush_block<T, NT, MODE>(a, cb, acc, r.xchg, s0, s1, G, c, s_last);
+      acc.zero();
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int mm = 0; mm < MP; ++mm) sacc[rr][mm] = 0.f;
+      ck = 0;
+      ++cb;
+    }
+  }
+  return true;
+}
+
+// ------------------------------------------------------------ host side
+inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+constexpr int kMaxCtasPerSm = 2;
+inline int64_t max_grid() { return static_cast<int64_t>(fd_host::sm_count()) * kMaxCtasPerSm; }
+
+// Workspace layout (fixed for a device, whatever the shape, so one buffer can
+// serve every launch):  [slots: max grid x 2 x BR x MT_MAX floats]
+//                       [counters: kMaxCounters ints][status word, padded to 256 B]
+//                       [MLP intermediates]
+inline size_t slots_bytes() { return align256(static_cast<size_t>(max_grid()) * 2 * BR * MT_MAX * sizeof(float)); }
+inline size_t counters_offset() { return slots_bytes(); }
+inline size_t status_offset() { return counters_offset() + kMaxCounters * sizeof(int); }
+inline size_t streamk_ws_bytes() { return status_offset() + 256; }
+
+struct Workspace {
+  float* slots;
+  int* counters;
+  int* status;
+  char* tail;
+};
+inline Workspace carve(void* ws) {
+  char* p = static_cast<char*>(ws);
+  return {reinterpret_cast<float*>(p), reinterpret_cast<int*>(p + counters_offset()),
+          reinterpret_cast<int*>(p + status_offset()), p + streamk_ws_bytes()};
+}
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Tensor map over 16-bit data: `rank` dims (innermost first) with byte strides
+// of the outer dims; boxes of 64 innermost elements, 128B swizzle, elements
+// outside the tensor read as 0.
+inline bool make_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                     const cuuint64_t* strides, const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, rank, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// [rows, cols] matrix with row stride `stride` elements, boxes of [box_rows x 64].
+inline bool make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride,
+                        int box_rows) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(KC), static_cast<cuuint32_t>(box_rows)};
+  return make_map(map, base, 2, dims, strides, box);
+}
+
+// w_gate_up [2i, h] (row stride s) as a 3-D [2][i][h] map: one [2 x 64 x 64]
+// box is 64 gate rows over the matching 64 up rows.
+inline bool make_gate_up_map(CUtensorMap* map, const void* w_gate_up, int64_t h, int64_t i, int64_t s) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(i), 2};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s) * 2, static_cast<cuuint64_t>(i) * s * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(KC), BR / 2, 2};
+  return make_map(map, w_gate_up, 3, dims, strides, box);
+}
+
+__host__ __device__ inline int x_slot_bytes(int m) { return m <= 8 ? 1024 : 2048; }
+
+__host__ __device__ inline size_t gateup_x_bytes(int m, int64_t ks, int boxes) {
+  return static_cast<size_t>(ks) * boxes * m * 128;
+}
+__host__ __device__ inline size_t linear_x_bytes(int m, int stages, int boxes) {
+  return static_cast<size_t>(stages) * boxes * x_slot_bytes(m);
+}
+inline size_t ring_smem_bytes(size_t xbytes, int stages, int boxes) {
+  return 1024 + static_cast<size_t>(stages) * boxes * BOX_BYTES + ((xbytes + 15) & ~static_cast<size_t>(15)) +
+         (BR / 2) * MT_MAX * 4 + 2 * MAX_STAGES * 8;
+}
+
+constexpr size_t kSmemPerSm = 228 * 1024;          // shared memory of one SM
+constexpr size_t kSmemPerCta = 227 * 1024 - 1024;  // opt-in maximum, less static shared memory
+
+// Pipeline geometry of one launch: CTAs per SM, producer warps, 64-column
+// boxes per step and ring stages.  Measured on B200 over the Llama-3-8B MLP
+// shapes (32-launch CUDA graphs, M = 1 and 8): one CTA per SM with two
+// producer warps, 32 KB steps (two boxes) and four stages streamed fastest
+// (gate/up 5.0 TB/s, down 4.5 TB/s); two CTAs per SM with one producer each
+// were 3-10% slower, 16 KB steps 20-30% slower.  `xbytes(stages, boxes)`
+// gives the X region the kernel needs.
+struct Geometry {
+  int ctas_per_sm, producers, boxes, stages;
+};
+
+template <typename XBytes>
+Geometry choose_geometry(XBytes xbytes) {
+  Geometry g{1, 2, 2, 4};
+  if (const char* env = std::getenv("FD_GEMV_GEOMETRY")) {  // tuning override: "cps,producers,boxes,stages"
+    int a = 0, b = 0, c = 0, d = 0;
+    if (std::sscanf(env, "%d,%d,%d,%d", &a, &b, &c, &d) == 4 && a >= 1 && a <= 2 && b >= 1 && b <= MAX_PRODUCERS &&
+        c >= 1 && c <= MAX_BOXES && d >= 2 && d <= MAX_STAGES)
+      g = {a, b, c, d};
+  }
+  const size_t per_cta = g.ctas_per_sm == 2 ? kSmemPerSm / 2 - 2048 : kSmemPerCta;
+  auto bytes = [&](int st) { return ring_smem_bytes(xbytes(st, g.boxes), st, g.boxes); };
+  while (g.stages > 2 && bytes(g.stages) > per_cta) --g.stages;
+  if (bytes(g.stages) > per_cta && g.ctas_per_sm == 2) {
+    // Two CTAs do not fit (a wide normalised batch): one CTA, two producers.
+    g.ctas_per_sm = 1;
+    g.producers = std::max(g.producers, 2);
+    g.stages = MAX_STAGES;
+    while (g.stages > 2 && bytes(g.stages) > kSmemPerCta) --g.stages;
+  }
+  if (g.ctas_per_sm == 2) g.producers = 1;  // the two-CTA kernels are built for 288 threads
+  g.stages -= g.stages % g.producers;       // every stage is always refilled by the same producer
+  if (g.stages < 2 || bytes(g.stages) > kSmemPerCta) g.stages = 0;
+  return g;
+}
+
+inline int from_cuda(cudaError_t e) { return e == cudaSuccess ? FD_OK : FD_ERR_LAUNCH; }
+
+}  // namespace fd_stream

@@ -325,6 +325,39 @@ def post_attn_mlp_out(
     _capi.check(status, "fd_post_attn_mlp_out")
 
 
+def post_attn_mlp_stack_out(
+    hidden2: torch.Tensor,
+    layers,
+    out2: torch.Tensor,
+    eps: float,
+    kind: str,
+) -> None:
+    """``len(layers)`` post_attn_mlp layers ``(norm_weight, w_gate_up, w_down)``
+    enqueued by one library call (two launches per layer); the last output
+    lands in ``out2``."""
+    if not layers:
+        raise ValueError("need at least one layer")
+    m, h = hidden2.shape
+    nw0, wgu0, wd0 = layers[0]
+    i = wd0.shape[1]
+    for nw, wgu, wd in layers:
+        if (wgu.shape != wgu0.shape or wd.shape != wd0.shape or wgu.stride() != wgu0.stride()
+                or wd.stride() != wd0.stride() or nw.dtype != nw0.dtype or nw.shape != nw0.shape):
+            raise ValueError("all layers must share shapes, strides and dtypes")
+    lib = _capi.load()
+    ws = WORKSPACES.get(hidden2.device, lib.fd_post_attn_mlp_workspace_bytes(m, h, i))
+    status = lib.fd_post_attn_mlp_stack_out(
+        hidden2.data_ptr(), len(layers),
+        _capi.ptr_array([nw.data_ptr() for nw, _, _ in layers]), _capi.dtype_code(nw0.dtype),
+        _capi.ptr_array([wgu.data_ptr() for _, wgu, _ in layers]), int(wgu0.stride(0)),
+        _capi.ptr_array([wd.data_ptr() for _, _, wd in layers]), int(wd0.stride(0)),
+        out2.data_ptr(), _capi.dtype_code(hidden2.dtype), m, h, i, float(eps),
+        _capi.FD_KIND_DOT if kind == "dot" else _capi.FD_KIND_SIMT,
+        ws.data_ptr(), ws.numel(), _capi.stream_of(hidden2),
+    )
+    _capi.check(status, "fd_post_attn_mlp_stack_out")
+
+
 def mlp_gate_up_out(
     hidden2: torch.Tensor,
     norm_weight: torch.Tensor,

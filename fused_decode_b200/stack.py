@@ -2,11 +2,13 @@
 
 The reference times ``post_attn_mlp`` inside a CUDA graph (bench.py:451-472)
 to take host launch cost out of the step.  ``MlpStack`` is that as a reusable
-object: it captures ``layers`` consecutive ``post_attn_mlp`` calls (two
-kernels each) on a private stream, and ``__call__`` copies the input into the
-graph's static buffer, replays, and returns the static output.  With
-``tp_group`` set it captures the tensor-parallel layer instead
-(``fused_decode_b200.tp``).
+object: it captures the whole stack on a private stream, and ``__call__``
+copies the input into the graph's static buffer, replays, and returns the
+static output.  By default the whole stack is enqueued by one library call
+(``fd_post_attn_mlp_stack_out``: two programmatic-dependent launches per
+layer, intermediates in the library workspace).  ``fused=False`` captures one
+``post_attn_mlp`` call per layer instead, and ``layer_fn`` captures any per-layer callable (the
+tensor-parallel layer of ``fused_decode_b200.tp``, for one).
 """
 
 from __future__ import annotations
@@ -35,6 +37,7 @@ class MlpStack:
         *,
         kind: str | None = None,
         layer_fn=None,
+        fused: bool | None = None,
     ) -> None:
         if not layers:
             raise ValueError("need at least one layer")
@@ -48,11 +51,20 @@ class MlpStack:
         self.dtype = wgu0.dtype
         self._fn = layer_fn or (lambda x, nw, wgu, wd: post_attn_mlp(x, nw, wgu, wd, self.eps, kind=self.kind))
         self.static_in = torch.zeros(batch, self.h, device=self.device, dtype=self.dtype)
+        can_fuse = layer_fn is None and all(
+            K.mlp_fusable(self.static_in, nw, wgu, wd) for nw, wgu, wd in self.layers)
+        if fused and not can_fuse:
+            raise ValueError("these layers cannot run as one fused stack")
+        self.fused = can_fuse if fused is None else bool(fused)
         self._stream = torch.cuda.Stream(device=self.device)
         self.graph = torch.cuda.CUDAGraph()
         self._capture()
 
     def _run(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fused:
+            out = torch.empty_like(x)
+            K.post_attn_mlp_stack_out(x, self.layers, out, self.eps, self.kind)
+            return out
         for nw, wgu, wd in self.layers:
             x = self._fn(x, nw, wgu, wd)
         return x
@@ -69,6 +81,7 @@ class MlpStack:
 
     @property
     def launches_per_replay(self) -> int:
+        """Kernel launches of this library per replay."""
         return 2 * len(self.layers)
 
     def replay(self) -> torch.Tensor:

@@ -97,8 +97,9 @@ size_t fd_linear_workspace_bytes(int32_t m, int64_t n, int64_t k);
 
 /* Byte offset, inside any workspace above, of a 32-bit status word the
  * kernels OR error bits into (1: a consumer's shared-memory pipeline wait
- * expired, 2: a producer's wait expired).  Zero means no error; the caller
- * resets it. */
+ * expired, 2: a producer's wait expired).  Zero means no error.  After a non-zero
+ * status the outputs of that launch are invalid and the workspace must be
+ * zero-filled again before reuse. */
 size_t fd_workspace_status_offset(void);
 
 /* y[m, n] = round(sum_k x[m, k] * w[n, k] + bias[n] + row_add[m, n]) for
@@ -123,12 +124,13 @@ size_t fd_post_attn_mlp_workspace_bytes(int32_t m, int64_t h, int64_t i);
  *   gate_up = round(normed @ w_gate_up^T)   (w_gate_up is [2i, h], gate above up)
  *   mid     = round(silu(gate) * up)
  *   out     = round(mid @ w_down^T + hidden)   (w_down is [h, i])
- * Two kernels instead of the reference's four launches.  add_residual = 0
- * drops "+ hidden"; out_dtype = FD_F32 stores the unrounded fp32 sum (a
- * tensor-parallel rank's partial before its allreduce), otherwise out_dtype
- * must equal dtype.  w_gate_up / w_down may carry any row stride that is a
- * multiple of 8 (k-stride 1); norm_w is f16, bf16 or f32.  The rounding points
- * follow post_attn_mlp_reference (reference reference.py:66-79).
+ * Two launches (RMSNorm + gate/up + SwiGLU, then down + residual; the second
+ * programmatic-dependent on the first) instead of the reference's four.  add_residual = 0 drops "+ hidden";
+ * out_dtype = FD_F32 stores the unrounded fp32 sum (a tensor-parallel rank's
+ * partial before its allreduce), otherwise out_dtype must equal dtype.
+ * w_gate_up / w_down may carry any row stride that is a multiple of 8
+ * (k-stride 1); norm_w is f16, bf16 or f32.  The rounding points follow
+ * post_attn_mlp_reference (reference reference.py:66-79).
  * Replaces post_attn_mlp's launches (reference ops.py:312-315). */
 int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dtype,
                          const void* w_gate_up, int64_t s_gu,
@@ -137,6 +139,21 @@ int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dt
                          int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
                          int32_t add_residual, void* workspace, size_t workspace_bytes,
                          void* stream);
+
+/* `layers` consecutive post_attn_mlp layers (layer l reads layer l-1's
+ * output): norm_w, w_gate_up and w_down are HOST arrays of `layers` device
+ * pointers with shared shapes, strides and dtypes.  Two launches per layer,
+ * enqueued by one call; intermediate activations live in the workspace and
+ * only the last layer's output is written to `out`.  The workspace is
+ * fd_post_attn_mlp_workspace_bytes(m, h, i).
+ * Replaces a loop of post_attn_mlp calls (reference ops.py:283-315). */
+int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers,
+                               const void* const* norm_w, int32_t norm_dtype,
+                               const void* const* w_gate_up, int64_t s_gu,
+                               const void* const* w_down, int64_t s_down,
+                               void* out, int32_t dtype, int32_t m, int64_t h, int64_t i,
+                               float eps, int32_t kind, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* First kernel of fd_post_attn_mlp_out on its own: mid[m, i] (contiguous) =
  * round(silu(gate) * up) of the RMSNorm'd hidden rows.  Replaces the

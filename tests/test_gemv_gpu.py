@@ -209,3 +209,64 @@ def test_zz_no_pipeline_timeouts():
     """No kernel in this module hit a bounded pipeline wait."""
     torch.cuda.synchronize()
     assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+
+
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_post_attn_mlp_stack_fused(m):
+    """Six layers from one stack call: equal to six single-layer calls bit for
+    bit, and to the chained oracle within tolerance."""
+    from fused_decode_b200.stack import MlpStack
+
+    h, i, layers = 512, 1024, 6
+    dtype = torch.bfloat16
+    ws = [_mlp_weights(h, i, dtype, 300 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(31 + m))
+    fused_out = torch.empty_like(x0)
+    K.post_attn_mlp_stack_out(x0, ws, fused_out, 1e-5, "dot")
+    x = x0
+    for nw, wgu, wd in ws:
+        x = post_attn_mlp(x, nw, wgu, wd, 1e-5)
+    assert torch.equal(fused_out, x)
+    ref = _np(x0)
+    for nw, wgu, wd in ws:
+        ref = O.post_attn_mlp(ref, _np(nw), _np(wgu), _np(wd), 1e-5, "bfloat16")
+    _close(fused_out, ref, {"rtol": 2e-2, "atol": 2e-2})
+    stack = MlpStack(ws, m, 1e-5, kind="dot")
+    assert stack.fused and stack.launches_per_replay == 2 * layers
+    for _ in range(2):
+        torch.testing.assert_close(stack(x0), fused_out, rtol=0, atol=0)
+
+
+def test_post_attn_mlp_stack_many_layers():
+    """35 layers: the ping-pong buffers alternate an odd number of times."""
+    h, i, layers, m = 128, 256, 35, 3
+    dtype = torch.float16
+    ws = [_mlp_weights(h, i, dtype, 400 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(77))
+    out = torch.empty_like(x0)
+    K.post_attn_mlp_stack_out(x0, ws, out, 1e-6, "dot")
+    x = x0
+    for nw, wgu, wd in ws:
+        x = post_attn_mlp(x, nw, wgu, wd)
+    assert torch.equal(out, x)
+
+
+def test_post_attn_mlp_stack_simt_and_fp32_norm():
+    h, i, layers, m = 256, 384, 4, 7
+    dtype = torch.float16
+    ws = []
+    for l in range(layers):
+        nw, wgu, wd = _mlp_weights(h, i, dtype, 500 + l)
+        ws.append((nw.float(), wgu, wd))
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(5))
+    out = torch.empty_like(x0)
+    K.post_attn_mlp_stack_out(x0, ws, out, 1e-6, "simt")
+    ref = _np(x0)
+    for nw, wgu, wd in ws:
+        ref = O.post_attn_mlp(ref, _np(nw), _np(wgu), _np(wd), 1e-6, "float16")
+    _close(out, ref, {"rtol": 2e-2, "atol": 2e-2})
+
+
+def test_zz_no_pipeline_timeouts_after_stacks():
+    torch.cuda.synchronize()
+    assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
