@@ -79,11 +79,17 @@ class TPPostAttnMlp:
                             self.kind, add_residual=False)
         return part
 
+    def finish(self, total: torch.Tensor, hidden2: torch.Tensor) -> torch.Tensor:
+        """``round(total + hidden)``: the allreduced fp32 sum plus the residual."""
+        out = torch.empty(hidden2.shape, device=hidden2.device, dtype=hidden2.dtype)
+        K.residual_add_out(total, hidden2, out)
+        return out
+
     def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
         h = hidden.shape[-1]
+        if self.w_gate_up.shape[1] != h:
+            raise ValueError(f"hidden width {h} does not match the weights' H={self.w_gate_up.shape[1]}")
         hidden2 = hidden.reshape(-1, h).contiguous()
         part = self.partial(hidden2)
         dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
-        out = torch.empty(hidden.shape, device=hidden.device, dtype=hidden.dtype)
-        K.residual_add_out(part, hidden2, out.view(-1, h))
-        return out
+        return self.finish(part, hidden2).view(hidden.shape)

@@ -6,10 +6,11 @@ inputs and outputs as ``golden.npz`` plus a ``manifest.json``.  The shapes
 follow the reference's tests (tests/test_ops.py:42-171) and the BASELINE
 configurations, scaled down so the fixtures stay small.
 
-This script needs the reference source tree (default ``/root/reference/src``,
-override with ``FUSED_DECODE_REF``) and is run by hand in the build container:
+This script needs the reference's ``src`` directory (the folder holding the
+``fused_decode`` package), named by ``FUSED_DECODE_REF``, and is run by hand
+in the build container:
 
-    python tests/golden/make_golden.py
+    FUSED_DECODE_REF=<reference checkout>/src python tests/golden/make_golden.py
 
 The GPU box never runs it; the committed fixtures travel instead.
 """
@@ -25,7 +26,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("FUSED_DECODE_REF", "/root/reference/src")
+REF = os.environ.get("FUSED_DECODE_REF")
+if not REF:
+    raise SystemExit("set FUSED_DECODE_REF to the reference's src directory")
 sys.path.insert(0, REF)
 
 from fused_decode import reference as R  # noqa: E402  (the reference's own oracle)
