@@ -280,6 +280,7 @@ def run_ours(args) -> None:
     def barrier():
         if world > 1:
             dist.barrier()
+            torch.cuda.synchronize()
 
     def max_over_ranks(v: float) -> float:
         if world == 1:
@@ -304,12 +305,11 @@ def run_ours(args) -> None:
         stack.static_in.copy_(x0)
         for _ in range(warmup):
             stack.replay()
-        torch.cuda.synchronize()
-        barrier()
         if sampler:
-            sampler.start()
+            sampler.start()  # before the barrier: every rank starts its clock together
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
+        barrier()
         t0 = time.perf_counter()
         s.record()
         for _ in range(steps):

@@ -6,7 +6,7 @@
 //    an equal contiguous piece of the flat step range [0, nblocks*KS), so
 //    every SM streams the same number of weight bytes whatever N and K are.
 //  * TMA ring.  P producer warps take turns issuing each step's B 2-D/3-D
-//    tensor-map loads (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//    tensor-map loads (cp.async.bulk.tensor, 128-byte swizzle, per-CTA tiles)
 //    of a [128 x 64] weight box -- and, for a plain GEMV, the [M x 64]
 //    activation boxes -- into an S-stage shared-memory ring guarded by
 //    mbarriers (full: data landed, empty: all consumer warps read it).
@@ -153,7 +153,7 @@ FD_DEV uint64_t evict_first_policy() {
   return p;
 }
 // 2-D / 3-D tiled TMA loads into this CTA's shared memory, completing on `bar`
-// (no multicast: every CTA fetches its own tiles).
+// (every CTA fetches its own tiles into its own shared memory).
 FD_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar, uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "

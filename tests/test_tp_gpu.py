@@ -4,8 +4,8 @@
   (the fused MLP kernels with an fp32 partial and no residual); the partials
   are summed in rank order and finished by ``residual_add_out`` -- the TP layer
   without the collective.  Compared with the oracle's partials summed the same
-  way (same fp32 values up to summation order inside the kernels), and with
-  the unsharded oracle layer within BASELINE's atol = rtol = 1e-2.
+  way (within one bf16 rounding step: rtol 2^-7, atol 1e-3), and with the
+  unsharded oracle layer within BASELINE's atol = rtol = 1e-2.
 * Two or more GPUs: ranks over NCCL run chained TP layers end to end
   (``TPPostAttnMlp.__call__``, one ``all_reduce`` per layer); skipped when the
   machine has fewer than two GPUs.
@@ -62,8 +62,11 @@ def test_tp_shards_one_gpu(world, m):
     assert out.dtype == x.dtype and out.shape == x.shape and out.is_contiguous()
     full = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), EPS, "bfloat16")
     torch.testing.assert_close(out.float().cpu(), torch.from_numpy(full), **TOL)
+    # The oracle's TP emulation: the same shards' partials summed in rank order.
+    # Kernel and oracle partials differ by fp32 summation order only, so the
+    # two agree to one bf16 rounding step (at most 2^-7 relative; absolute near zero).
     emul = O.round_to(ref_total + _np(x), "bfloat16")
-    assert np.abs(O.ulp_distance(_np(out), emul, "bfloat16")).max() <= 1
+    torch.testing.assert_close(out.float().cpu(), torch.from_numpy(emul), rtol=2 ** -7, atol=1e-3)
 
 
 def _free_port():
