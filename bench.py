@@ -256,6 +256,112 @@ def copy_roof_gbs(torch, device) -> float:
     return 2 * n * 2 / (ms * 1e-3) / 1e9
 
 
+L2_BYTES = 126 * 1024 * 1024
+GEMV_SHAPES = ((4096, 4096), (14336, 4096), (4096, 14336), (28672, 4096))
+GEMV_MS = (1, 2, 4, 8, 16)
+
+
+def graph_time_us(torch, calls, reps: int = 3, inner: int = 20) -> float:
+    """Device time per call (us) of a rotation of `calls` replayed in a CUDA
+    graph of `inner` calls; median of `reps` timed replays after 3 warm-up."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for c in calls:
+            c()
+    torch.cuda.current_stream().wait_stream(stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for j in range(inner):
+            calls[j % len(calls)]()
+    for _ in range(3):
+        g.replay()
+    times = [cuda_time(torch, g.replay, 1) for _ in range(reps)]
+    del g
+    return statistics.median(times) * 1e3 / inner
+
+
+def copies_for(nbytes: int) -> int:
+    """Input copies to rotate so one pass touches at least 2x L2."""
+    return max(1, -(-2 * L2_BYTES // max(nbytes, 1)))
+
+
+def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
+    """Standalone ops at the BASELINE shapes: us per call, algorithmic GB/s and
+    fractions of the in-process copy roof and of the measured peak."""
+    import fused_decode_b200 as fd
+
+    g = torch.Generator(device=device).manual_seed(0)
+    out: dict = {}
+
+    def rec(name, us, nbytes, **extra):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us": us, "bytes": nbytes, "gbs": gbs, "frac_copy_roof": gbs / roof_gbs,
+                     "frac_peak": gbs / peak_gbs, **extra}
+
+    f16 = torch.float16
+    # add+RMSNorm and RMSNorm (BASELINE config 0)
+    for rows in (8192, 1):
+        w = (1 + 0.1 * torch.randn(H, device=device, generator=g)).to(f16)
+        n_add = 4 * rows * H * 2 + H * 2
+        k = copies_for(n_add)
+        xs = [torch.randn(rows, H, device=device, dtype=f16, generator=g) for _ in range(k)]
+        rs = [torch.randn(rows, H, device=device, dtype=f16, generator=g) for _ in range(k)]
+        os_ = [torch.empty(rows, H, device=device, dtype=f16) for _ in range(k)]
+        calls = [(lambda j=j: fd.add_rms_norm(xs[j], rs[j], w, 1e-5, out=os_[j], residual_out=rs[j]))
+                 for j in range(k)]
+        rec(f"add_rms_norm_{rows}x{H}_f16", graph_time_us(torch, calls), n_add)
+        n_rms = 2 * rows * H * 2 + H * 2
+        calls = [(lambda j=j: fd.rms_norm(xs[j], w, 1e-5, out=os_[j])) for j in range(k)]
+        rec(f"rms_norm_{rows}x{H}_f16", graph_time_us(torch, calls), n_rms)
+        del xs, rs, os_
+    # SwiGLU (config 1)
+    for rows in (2048, 1):
+        for dt, tag in ((f16, "f16"), (torch.bfloat16, "bf16")):
+            nb = 3 * rows * I * 2
+            k = copies_for(nb)
+            gs = [torch.randn(rows, I, device=device, dtype=dt, generator=g) for _ in range(k)]
+            us_ = [torch.randn(rows, I, device=device, dtype=dt, generator=g) for _ in range(k)]
+            os_ = [torch.empty(rows, I, device=device, dtype=dt) for _ in range(k)]
+            calls = [(lambda j=j: fd.swiglu(gs[j], us_[j], out=os_[j])) for j in range(k)]
+            rec(f"swiglu_{rows}x{I}_{tag}", graph_time_us(torch, calls), nb)
+            del gs, us_, os_
+    # RoPE (config 1): x [1, T, 32, 128], cos/sin [T, 1, 128] from theta = 500000
+    for t in (2048, 1):
+        cos, sin = rope_tables(torch, t, 128, device, f16)
+        nb = 2 * t * 32 * 128 * 2 + 2 * t * 128 * 2
+        k = copies_for(nb)
+        xs = [torch.randn(1, t, 32, 128, device=device, dtype=f16, generator=g) for _ in range(k)]
+        os_ = [torch.empty_like(xs[0]) for _ in range(k)]
+        calls = [(lambda j=j: fd.rope(xs[j], cos, sin, out=os_[j])) for j in range(k)]
+        rec(f"rope_1x{t}x32x128_f16", graph_time_us(torch, calls), nb)
+        del xs, os_
+    # linear_decode sweep (config 2); weights rotate through >= 2x L2
+    for dt, tag in ((torch.bfloat16, "bf16"), (f16, "f16")):
+        for n, kk in GEMV_SHAPES:
+            k = copies_for(n * kk * 2)
+            ws = [(torch.randn(n, kk, device=device, generator=g) * 0.02).to(dt) for _ in range(k)]
+            for m in GEMV_MS:
+                x = torch.randn(m, kk, device=device, dtype=dt, generator=g)
+                y = torch.empty(m, n, device=device, dtype=dt)
+                calls = [(lambda j=j: fd.linear_decode(x, ws[j], out=y, kind="dot")) for j in range(k)]
+                nb = (m * kk + n * kk + m * n) * 2
+                rec(f"linear_decode_m{m}_n{n}_k{kk}_{tag}", graph_time_us(torch, calls), nb)
+            if n == 4096 and kk == 14336:  # the down projection with bias + row_add
+                for m in (1, 8):
+                    x = torch.randn(m, kk, device=device, dtype=dt, generator=g)
+                    b = (torch.randn(n, device=device, generator=g) * 0.02).to(dt)
+                    ra = torch.randn(m, n, device=device, dtype=dt, generator=g)
+                    y = torch.empty(m, n, device=device, dtype=dt)
+                    calls = [(lambda j=j: fd.linear_decode(x, ws[j], b, row_add=ra, out=y, kind="dot"))
+                             for j in range(k)]
+                    nb = (m * kk + n * kk + 2 * m * n + n) * 2
+                    rec(f"linear_decode_m{m}_n{n}_k{kk}_{tag}_bias_rowadd", graph_time_us(torch, calls), nb)
+            del ws
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -451,6 +557,10 @@ def run_ours(args) -> None:
                "sample": f"{evals} layer evaluations over 2 seeded Llama-3-8B MLP layers at M={args.m} "
                          f"(numpy fp32 oracle port of reference.py:66-79), ~{args.cpu_seconds:.0f} s"}
 
+    ops = None
+    if world == 1 and not args.no_ops:
+        ops = run_ops(torch, device, roof, pk["hbm_gbs"])
+
     if rank == 0:
         traffic = committed_traffic().get(f"gate_up_kernel_bytes_per_launch_m{args.m}") if world == 1 else None
         gbs1 = bytes1 / (us1 * 1e-6) / 1e9
@@ -496,6 +606,7 @@ def run_ours(args) -> None:
                 "per_layer_calls_us_per_layer": per_layer_us,
                 "two_kernel_us_per_layer": two_kernel_us,
             },
+            "ops": ops,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_s * 1e6 / LAYERS, "unit": "us/layer",
                     "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
@@ -586,6 +697,7 @@ def main() -> None:
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ops", action="store_true", help="skip the standalone-op measurements")
     ap.add_argument("--ncu-case", choices=NCU_CASES, default=None,
                     help="run a small fixed workload of one kernel for an ncu capture and exit")
     args = ap.parse_args()

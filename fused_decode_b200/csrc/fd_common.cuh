@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/fd_b200.h"
 
 #define FD_DEV __device__ __forceinline__
@@ -141,6 +143,26 @@ FD_DEV int64_t row_base(int64_t row, int64_t B, int64_t C, int64_t sa, int64_t s
   return a * sa + b * sb + c * sc;
 }
 
+// silu(g) * u with the stable sigmoid of the reference kernel
+// (kernels.py:448-451): e = exp(-|g|); sigmoid = 1/(1+e) for g >= 0, else
+// e/(1+e).  exp and the reciprocal are the hardware approximations (__expf,
+// __fdividef with a divisor in [1, 2]): a few fp32 ulp, far below the one
+// rounding to the 16-bit output, and cheap enough that a streaming SwiGLU
+// stays bound by HBM rather than by the IEEE divide.
+FD_DEV float silu_mul(float g, float u) {
+  const float e = __expf(-fabsf(g));
+  const float r = __fdividef(1.0f, 1.0f + e);
+  return g * (g >= 0.f ? r : e * r) * u;
+}
+
+// ------------------------------------------------- programmatic dependent launch
+// Kernels launched with fd_host::launch_pdl may start while the previous
+// kernel on the stream is still draining.  Every such kernel calls
+// grid_dep_wait() before its first access to global memory another kernel may
+// have written, and grid_dep_launch() once the next kernel may be scheduled.
+FD_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+FD_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- reductions
 FD_DEV float warp_sum(float v) {
 #pragma unroll
@@ -179,5 +201,23 @@ inline bool same_grid(const fd_rows* l, const fd_rows* r) {
 }
 
 int sm_count();
+
+// Launch `kernel` on `stream` as a programmatic dependent of the previous
+// kernel in the stream (see grid_dep_wait).
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace fd_host

@@ -6,6 +6,8 @@
 #include "fd_common.cuh"
 
 #include <algorithm>
+#include <mutex>
+#include <unordered_map>
 
 using namespace fd;
 
@@ -49,6 +51,7 @@ FD_DEV T* row_ptr(const RowsArg& g, int64_t row, int64_t B, int64_t C) {
 struct RmsArgs {
   RowsArg x, r, y, ro;
   int64_t B, C, rows;
+  int32_t flat;  // the grid has one leading dimension
   const void* w;
   int32_t w_dtype;
   int32_t wpr;   // warps per row
@@ -58,7 +61,24 @@ struct RmsArgs {
   float eps;
 };
 
-template <typename T, int VPT, bool HAS_RES, bool STORE_RES>
+// Element offset of row `row` in a row grid.  FLAT: a 2-D grid (one leading
+// dimension).  Otherwise the (ia, ib, ic) split in 32-bit arithmetic (the host
+// sends grids of 2^32 rows or more to the generic kernel).
+struct RowIdx {
+  uint32_t ia, ib, ic;
+};
+template <bool FLAT>
+FD_DEV RowIdx split_row(int64_t row, int64_t B, int64_t C) {
+  if (FLAT) return {0u, 0u, static_cast<uint32_t>(row)};
+  const uint32_t r = static_cast<uint32_t>(row), c = static_cast<uint32_t>(C), b = static_cast<uint32_t>(B);
+  const uint32_t t = r / c;
+  return {t / b, t % b, r % c};
+}
+FD_DEV int64_t offset_of(const RowsArg& g, const RowIdx& i) {
+  return i.ia * g.sa + i.ib * g.sb + static_cast<int64_t>(i.ic) * g.sc;
+}
+
+template <typename T, int VPT, bool HAS_RES, bool STORE_RES, bool FLAT>
 __global__ void __launch_bounds__(512) rms_vec_kernel(RmsArgs a) {
   __shared__ float red[32];
   const int group_threads = 32 * a.wpr;
@@ -66,12 +86,15 @@ __global__ void __launch_bounds__(512) rms_vec_kernel(RmsArgs a) {
   const int t = threadIdx.x - group * group_threads;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rpc + group;
   const bool live = row < a.rows;
+  const RowIdx ri = split_row<FLAT>(live ? row : 0, a.B, a.C);
+  grid_dep_wait();
+  grid_dep_launch();
 
   float s[VPT][8];
   float sumsq = 0.f;
   if (live) {
-    const T* xr = row_ptr<T>(a.x, row, a.B, a.C);
-    const T* rr = HAS_RES ? row_ptr<T>(a.r, row, a.B, a.C) : nullptr;
+    const T* xr = reinterpret_cast<const T*>(a.x.ptr) + offset_of(a.x, ri);
+    const T* rr = HAS_RES ? reinterpret_cast<const T*>(a.r.ptr) + offset_of(a.r, ri) : nullptr;
     uint4 xv[VPT], rv[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -97,7 +120,7 @@ __global__ void __launch_bounds__(512) rms_vec_kernel(RmsArgs a) {
       }
     }
     if (STORE_RES) {
-      T* ror = row_ptr<T>(a.ro, row, a.B, a.C);
+      T* ror = reinterpret_cast<T*>(a.ro.ptr) + offset_of(a.ro, ri);
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int j = t + i * group_threads;
@@ -116,7 +139,7 @@ __global__ void __launch_bounds__(512) rms_vec_kernel(RmsArgs a) {
   }
   if (!live) return;
   const float inv = 1.0f / sqrtf(sumsq / static_cast<float>(a.n) + a.eps);
-  T* yr = row_ptr<T>(a.y, row, a.B, a.C);
+  T* yr = reinterpret_cast<T*>(a.y.ptr) + offset_of(a.y, ri);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int j = t + i * group_threads;
@@ -149,6 +172,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) rms_generic_kernel(RmsGenArgs a) {
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
+  grid_dep_wait();
+  grid_dep_launch();
   const T* xr = row_ptr<T>(a.x, row, a.B, a.C);
   const T* rr = a.has_res ? row_ptr<T>(a.r, row, a.B, a.C) : nullptr;
   float sumsq = 0.f;
@@ -174,19 +199,21 @@ __global__ void __launch_bounds__(256) rms_generic_kernel(RmsGenArgs a) {
   }
 }
 
+template <typename T, int VPT, bool FLAT>
+cudaError_t launch_rms_vec2(const RmsArgs& a, bool has_res, bool store_res, cudaStream_t st) {
+  const dim3 threads(32 * a.wpr * a.rpc);
+  const dim3 blocks(static_cast<unsigned>((a.rows + a.rpc - 1) / a.rpc));
+  using fd_host::launch_pdl;
+  if (has_res && store_res) return launch_pdl(rms_vec_kernel<T, VPT, true, true, FLAT>, blocks, threads, 0, st, a);
+  if (has_res) return launch_pdl(rms_vec_kernel<T, VPT, true, false, FLAT>, blocks, threads, 0, st, a);
+  if (store_res) return launch_pdl(rms_vec_kernel<T, VPT, false, true, FLAT>, blocks, threads, 0, st, a);
+  return launch_pdl(rms_vec_kernel<T, VPT, false, false, FLAT>, blocks, threads, 0, st, a);
+}
+
 template <typename T, int VPT>
 cudaError_t launch_rms_vec(const RmsArgs& a, bool has_res, bool store_res, cudaStream_t st) {
-  const int threads = 32 * a.wpr * a.rpc;
-  const unsigned blocks = static_cast<unsigned>((a.rows + a.rpc - 1) / a.rpc);
-  if (has_res && store_res)
-    rms_vec_kernel<T, VPT, true, true><<<blocks, threads, 0, st>>>(a);
-  else if (has_res)
-    rms_vec_kernel<T, VPT, true, false><<<blocks, threads, 0, st>>>(a);
-  else if (store_res)
-    rms_vec_kernel<T, VPT, false, true><<<blocks, threads, 0, st>>>(a);
-  else
-    rms_vec_kernel<T, VPT, false, false><<<blocks, threads, 0, st>>>(a);
-  return cudaGetLastError();
+  return a.flat ? launch_rms_vec2<T, VPT, true>(a, has_res, store_res, st)
+                : launch_rms_vec2<T, VPT, false>(a, has_res, store_res, st);
 }
 
 template <typename T>
@@ -222,27 +249,27 @@ struct SwigluArgs {
   int64_t items;  // rows * nv (vector path) or rows * n (scalar path)
 };
 
-FD_DEV float silu_mul(float g, float u) {
-  // Stable sigmoid, as the reference kernel computes it (kernels.py:448-451).
-  const float e = expf(-fabsf(g));
-  const float sig = g >= 0.f ? 1.0f / (1.0f + e) : e / (1.0f + e);
-  return g * sig * u;
-}
-
-template <typename T, bool FLAT>
+// I is the index type of the item -> (row, vector) split: 32-bit whenever the
+// item count fits, which keeps the per-item divisions cheap.
+template <typename T, bool FLAT, typename I>
 __global__ void __launch_bounds__(256) swiglu_vec_kernel(SwigluArgs a) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < a.items;
-       it += stride) {
-    const int64_t row = it / a.nv;
-    const int64_t j = it - row * a.nv;
+  grid_dep_wait();
+  grid_dep_launch();
+  const I stride = static_cast<I>(gridDim.x) * blockDim.x;
+  const I items = static_cast<I>(a.items), nv = static_cast<I>(a.nv);
+  for (I it = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
+    const I row = it / nv;
+    const int64_t j = it - row * nv;
     int64_t og, ou, oy;
     if (FLAT) {
-      og = row * a.g.sc; ou = row * a.u.sc; oy = row * a.y.sc;
+      og = static_cast<int64_t>(row) * a.g.sc; ou = static_cast<int64_t>(row) * a.u.sc;
+      oy = static_cast<int64_t>(row) * a.y.sc;
     } else {
-      og = row_base(row, a.B, a.C, a.g.sa, a.g.sb, a.g.sc);
-      ou = row_base(row, a.B, a.C, a.u.sa, a.u.sb, a.u.sc);
-      oy = row_base(row, a.B, a.C, a.y.sa, a.y.sb, a.y.sc);
+      const I C = static_cast<I>(a.C), B = static_cast<I>(a.B);
+      const I ic = row % C, t = row / C, ib = t % B, ia = t / B;
+      og = ia * a.g.sa + ib * a.g.sb + ic * a.g.sc;
+      ou = ia * a.u.sa + ib * a.u.sb + ic * a.u.sc;
+      oy = ia * a.y.sa + ib * a.y.sb + ic * a.y.sc;
     }
     const uint4 gv = ld_stream16(reinterpret_cast<const T*>(a.g.ptr) + og + 8 * j);
     const uint4 uv = ld_stream16(reinterpret_cast<const T*>(a.u.ptr) + ou + 8 * j);
@@ -257,6 +284,8 @@ __global__ void __launch_bounds__(256) swiglu_vec_kernel(SwigluArgs a) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) swiglu_generic_kernel(SwigluArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < a.items;
        it += stride) {
@@ -269,6 +298,25 @@ __global__ void __launch_bounds__(256) swiglu_generic_kernel(SwigluArgs a) {
   }
 }
 
+unsigned fill_blocks(const void* kernel, int64_t items, int threads);
+bool narrow_items(int64_t items);
+
+// A grid-stride kernel over a.items, one full wave of CTAs, PDL launch.
+template <typename Args>
+cudaError_t launch_stream(void (*kernel)(Args), const Args& a, int64_t items, cudaStream_t st) {
+  const unsigned blocks = fill_blocks(reinterpret_cast<const void*>(kernel), items, 256);
+  return fd_host::launch_pdl(kernel, blocks, 256, 0, st, a);
+}
+
+template <typename T>
+cudaError_t launch_swiglu_vec(const SwigluArgs& a, bool flat, cudaStream_t st) {
+  const bool narrow = narrow_items(a.items);
+  if (flat && narrow) return launch_stream(swiglu_vec_kernel<T, true, uint32_t>, a, a.items, st);
+  if (flat) return launch_stream(swiglu_vec_kernel<T, true, int64_t>, a, a.items, st);
+  if (narrow) return launch_stream(swiglu_vec_kernel<T, false, uint32_t>, a, a.items, st);
+  return launch_stream(swiglu_vec_kernel<T, false, int64_t>, a, a.items, st);
+}
+
 // ============================================================== RoPE
 struct RopeArgs {
   RowsArg x, c, s, y;
@@ -279,45 +327,68 @@ struct RopeArgs {
   int64_t items;
 };
 
-template <typename T>
+// Eight RoPE angles (cos or sin) of element type CT, kept packed until used.
+template <typename CT>
+struct Angles8 {
+  uint4 v;
+  FD_DEV void load(const CT* p) { v = __ldg(reinterpret_cast<const uint4*>(p)); }
+  FD_DEV float2 pair(int w) const { return unpack2<CT>(w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w); }
+};
+template <>
+struct Angles8<float> {
+  float4 lo, hi;
+  FD_DEV void load(const float* p) {
+    lo = __ldg(reinterpret_cast<const float4*>(p));
+    hi = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+  FD_DEV float2 pair(int w) const {
+    return w == 0 ? make_float2(lo.x, lo.y) : w == 1 ? make_float2(lo.z, lo.w)
+         : w == 2 ? make_float2(hi.x, hi.y) : make_float2(hi.z, hi.w);
+  }
+};
+
+// Vector path: one item = 8 elements of each half of one row.  CT is the
+// element type of cos and sin (one type for both here).
+template <typename T, typename CT, typename I>
 __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int ces = a.c_dtype == FD_F32 ? 4 : 2;
-  const int ses = a.s_dtype == FD_F32 ? 4 : 2;
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < a.items;
-       it += stride) {
-    const int64_t row = it / a.hv;
-    const int64_t j = 8 * (it - row * a.hv);
-    const int64_t ic = row % a.C;
-    const int64_t tt = row / a.C;
-    const int64_t ib = tt % a.B;
-    const int64_t ia = tt / a.B;
-    const int64_t ox = ia * a.x.sa + ib * a.x.sb + ic * a.x.sc;
-    const int64_t oc = ia * a.c.sa + ib * a.c.sb + ic * a.c.sc;
-    const int64_t os = ia * a.s.sa + ib * a.s.sb + ic * a.s.sc;
-    const int64_t oy = ia * a.y.sa + ib * a.y.sb + ic * a.y.sc;
-    const T* xp = reinterpret_cast<const T*>(a.x.ptr) + ox;
-    float x1[8], x2[8], c1[8], c2[8], s1[8], s2[8];
-    unpack8<T>(ld_stream16(xp + j), x1);
-    unpack8<T>(ld_stream16(xp + a.half + j), x2);
-    load8_as_f32(a.c.ptr + (oc + j) * ces, a.c_dtype, c1);
-    load8_as_f32(a.c.ptr + (oc + a.half + j) * ces, a.c_dtype, c2);
-    load8_as_f32(a.s.ptr + (os + j) * ses, a.s_dtype, s1);
-    load8_as_f32(a.s.ptr + (os + a.half + j) * ses, a.s_dtype, s2);
-    float o1[8], o2[8];
+  grid_dep_wait();
+  grid_dep_launch();
+  const I stride = static_cast<I>(gridDim.x) * blockDim.x;
+  const I items = static_cast<I>(a.items), hv = static_cast<I>(a.hv);
+  const I C = static_cast<I>(a.C), B = static_cast<I>(a.B);
+  for (I it = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
+    const I row = it / hv;
+    const int64_t j = 8 * static_cast<int64_t>(it - row * hv);
+    const I ic = row % C, tt = row / C, ib = tt % B, ia = tt / B;
+    const T* xp = reinterpret_cast<const T*>(a.x.ptr) + (ia * a.x.sa + ib * a.x.sb + ic * a.x.sc);
+    const CT* cp = reinterpret_cast<const CT*>(a.c.ptr) + (ia * a.c.sa + ib * a.c.sb + ic * a.c.sc);
+    const CT* sp = reinterpret_cast<const CT*>(a.s.ptr) + (ia * a.s.sa + ib * a.s.sb + ic * a.s.sc);
+    T* yp = reinterpret_cast<T*>(a.y.ptr) + (ia * a.y.sa + ib * a.y.sb + ic * a.y.sc);
+    const uint4 x1 = ld_stream16(xp + j);
+    const uint4 x2 = ld_stream16(xp + a.half + j);
+    Angles8<CT> c1, c2, s1, s2;
+    c1.load(cp + j);
+    c2.load(cp + a.half + j);
+    s1.load(sp + j);
+    s2.load(sp + a.half + j);
+    const uint32_t xw1[4] = {x1.x, x1.y, x1.z, x1.w}, xw2[4] = {x2.x, x2.y, x2.z, x2.w};
+    uint32_t o1[4], o2[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      o1[e] = x1[e] * c1[e] - x2[e] * s1[e];
-      o2[e] = x2[e] * c2[e] + x1[e] * s2[e];
+    for (int w = 0; w < 4; ++w) {
+      const float2 a1 = unpack2<T>(xw1[w]), a2 = unpack2<T>(xw2[w]);
+      const float2 cc1 = c1.pair(w), cc2 = c2.pair(w), ss1 = s1.pair(w), ss2 = s2.pair(w);
+      o1[w] = pack2<T>(a1.x * cc1.x - a2.x * ss1.x, a1.y * cc1.y - a2.y * ss1.y);
+      o2[w] = pack2<T>(a2.x * cc2.x + a1.x * ss2.x, a2.y * cc2.y + a1.y * ss2.y);
     }
-    T* yp = reinterpret_cast<T*>(a.y.ptr) + oy;
-    st_stream16(yp + j, pack8<T>(o1));
-    st_stream16(yp + a.half + j, pack8<T>(o2));
+    st_stream16(yp + j, make_uint4(o1[0], o1[1], o1[2], o1[3]));
+    st_stream16(yp + a.half + j, make_uint4(o2[0], o2[1], o2[2], o2[3]));
   }
 }
 
 template <typename T>
 __global__ void __launch_bounds__(256) rope_generic_kernel(RopeArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < a.items;
        it += stride) {
@@ -336,6 +407,18 @@ __global__ void __launch_bounds__(256) rope_generic_kernel(RopeArgs a) {
     yp[j * a.y.col] = from_f32<T>(x1 * c1 - x2 * s1);
     yp[(j + a.half) * a.y.col] = from_f32<T>(x2 * c2 + x1 * s2);
   }
+}
+
+template <typename T, typename CT>
+cudaError_t launch_rope_vec2(const RopeArgs& a, cudaStream_t st) {
+  return narrow_items(a.items) ? launch_stream(rope_vec_kernel<T, CT, uint32_t>, a, a.items, st)
+                               : launch_stream(rope_vec_kernel<T, CT, int64_t>, a, a.items, st);
+}
+template <typename T>
+cudaError_t launch_rope_vec(const RopeArgs& a, int cs_dtype, cudaStream_t st) {
+  if (cs_dtype == FD_F32) return launch_rope_vec2<T, float>(a, st);
+  if (cs_dtype == FD_BF16) return launch_rope_vec2<T, __nv_bfloat16>(a, st);
+  return launch_rope_vec2<T, __half>(a, st);
 }
 
 // ============================================================== copy / triad
@@ -391,10 +474,36 @@ template <typename T>
 __global__ void __launch_bounds__(256) residual_add_kernel(const float* __restrict__ partial,
                                                            const T* __restrict__ res, T* __restrict__ out,
                                                            int64_t n) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
     out[i] = from_f32<T>(partial[i] + to_f32(res[i]));
 }
+
+// CTAs of `threads` threads for a grid-stride kernel over `items`: as many as
+// are resident at once (one full wave, no tail wave), fewer for small inputs.
+unsigned fill_blocks(const void* kernel, int64_t items, int threads) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> per_sm;
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = per_sm.find(kernel);
+    if (it == per_sm.end()) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, 0) != cudaSuccess || occ < 1) occ = 1;
+      per_sm.emplace(kernel, occ);
+    } else {
+      occ = it->second;
+    }
+  }
+  const int64_t cap = static_cast<int64_t>(fd_host::sm_count()) * occ;
+  const int64_t need = std::max<int64_t>(1, (items + threads - 1) / threads);
+  return static_cast<unsigned>(std::min(need, cap));
+}
+
+// True when a 32-bit grid-stride index over `items` cannot overflow.
+bool narrow_items(int64_t items) { return items + static_cast<int64_t>(fd_host::sm_count()) * 2048 < (int64_t{1} << 32); }
 
 unsigned stream_blocks(int64_t items, int threads) {
   // Enough CTAs to fill every SM with 2048 threads, grid-striding beyond that.
@@ -457,9 +566,9 @@ int fd_rms_out(const fd_rows* x, const fd_rows* residual, const void* weight, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = x->dtype == FD_BF16;
 
-  const bool vec = (x->n % 8 == 0) && x->n <= 32768 && rows_vec16(x) && rows_vec16(out) &&
-                   (!has_res || rows_vec16(residual)) && (!store_res || rows_vec16(residual_out)) &&
-                   w_stride == 1 && aligned16(weight);
+  const bool vec = (x->n % 8 == 0) && x->n <= 32768 && rows < (int64_t{1} << 31) && rows_vec16(x) &&
+                   rows_vec16(out) && (!has_res || rows_vec16(residual)) &&
+                   (!store_res || rows_vec16(residual_out)) && w_stride == 1 && aligned16(weight);
   if (vec) {
     RmsArgs a;
     a.x = rows_arg(x); a.r = rows_arg(has_res ? residual : x);
@@ -468,6 +577,7 @@ int fd_rms_out(const fd_rows* x, const fd_rows* residual, const void* weight, in
     a.w = weight; a.w_dtype = w_dtype;
     a.nv = static_cast<int32_t>(x->n / 8); a.n = static_cast<int32_t>(x->n);
     a.eps = eps; a.wpr = 1; a.rpc = 1;
+    a.flat = x->a == 1 && x->b == 1;
     cudaError_t e = bf ? dispatch_rms_vec<__nv_bfloat16>(a, has_res, store_res, st)
                        : dispatch_rms_vec<__half>(a, has_res, store_res, st);
     return from_cuda(e);
@@ -479,11 +589,11 @@ int fd_rms_out(const fd_rows* x, const fd_rows* residual, const void* weight, in
   g.w = weight; g.w_dtype = w_dtype; g.w_stride = w_stride;
   g.n = x->n; g.eps = eps; g.has_res = has_res; g.store_res = store_res;
   if (rows > 0x7fffffffLL) return FD_ERR_UNSUPPORTED;
-  if (bf)
-    rms_generic_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), 256, 0, st>>>(g);
-  else
-    rms_generic_kernel<__half><<<static_cast<unsigned>(rows), 256, 0, st>>>(g);
-  return from_cuda(cudaGetLastError());
+  using fd_host::launch_pdl;
+  const dim3 blocks(static_cast<unsigned>(rows));
+  const cudaError_t e = bf ? launch_pdl(rms_generic_kernel<__nv_bfloat16>, blocks, 256, 0, st, g)
+                           : launch_pdl(rms_generic_kernel<__half>, blocks, 256, 0, st, g);
+  return from_cuda(e);
 }
 
 int fd_swiglu_out(const fd_rows* gate, const fd_rows* up, const fd_rows* out, void* stream) {
@@ -503,22 +613,14 @@ int fd_swiglu_out(const fd_rows* gate, const fd_rows* up, const fd_rows* out, vo
     a.nv = gate->n / 8;
     a.items = rows * a.nv;
     const bool flat = gate->a == 1 && gate->b == 1;
-    const unsigned blocks = stream_blocks(a.items, 256);
-    if (bf) {
-      if (flat) swiglu_vec_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>(a);
-      else swiglu_vec_kernel<__nv_bfloat16, false><<<blocks, 256, 0, st>>>(a);
-    } else {
-      if (flat) swiglu_vec_kernel<__half, true><<<blocks, 256, 0, st>>>(a);
-      else swiglu_vec_kernel<__half, false><<<blocks, 256, 0, st>>>(a);
-    }
-    return from_cuda(cudaGetLastError());
+    const cudaError_t e = bf ? launch_swiglu_vec<__nv_bfloat16>(a, flat, st) : launch_swiglu_vec<__half>(a, flat, st);
+    return from_cuda(e);
   }
   a.nv = 0;
   a.items = rows * gate->n;
-  const unsigned blocks = stream_blocks(a.items, 256);
-  if (bf) swiglu_generic_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
-  else swiglu_generic_kernel<__half><<<blocks, 256, 0, st>>>(a);
-  return from_cuda(cudaGetLastError());
+  const cudaError_t e = bf ? launch_stream(swiglu_generic_kernel<__nv_bfloat16>, a, a.items, st)
+                           : launch_stream(swiglu_generic_kernel<__half>, a, a.items, st);
+  return from_cuda(e);
 }
 
 int fd_rope_out(const fd_rows* x, const fd_rows* cos, const fd_rows* sin, const fd_rows* out,
@@ -538,22 +640,20 @@ int fd_rope_out(const fd_rows* x, const fd_rows* cos, const fd_rows* sin, const 
   a.c_dtype = cos->dtype; a.s_dtype = sin->dtype;
   a.B = x->b; a.C = x->c; a.rows = rows;
   a.half = x->n / 2;
-  const bool vec = a.half % 8 == 0 && rows_vec16(x) && rows_vec16(cos) && rows_vec16(sin) &&
-                   rows_vec16(out);
+  const bool vec = a.half % 8 == 0 && cos->dtype == sin->dtype && rows_vec16(x) && rows_vec16(cos) &&
+                   rows_vec16(sin) && rows_vec16(out);
   if (vec) {
     a.hv = a.half / 8;
     a.items = rows * a.hv;
-    const unsigned blocks = stream_blocks(a.items, 256);
-    if (bf) rope_vec_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
-    else rope_vec_kernel<__half><<<blocks, 256, 0, st>>>(a);
-    return from_cuda(cudaGetLastError());
+    const cudaError_t e = bf ? launch_rope_vec<__nv_bfloat16>(a, cos->dtype, st)
+                             : launch_rope_vec<__half>(a, cos->dtype, st);
+    return from_cuda(e);
   }
   a.hv = 0;
   a.items = rows * a.half;
-  const unsigned blocks = stream_blocks(a.items, 256);
-  if (bf) rope_generic_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
-  else rope_generic_kernel<__half><<<blocks, 256, 0, st>>>(a);
-  return from_cuda(cudaGetLastError());
+  const cudaError_t e = bf ? launch_stream(rope_generic_kernel<__nv_bfloat16>, a, a.items, st)
+                           : launch_stream(rope_generic_kernel<__half>, a, a.items, st);
+  return from_cuda(e);
 }
 
 int fd_residual_add_out(const float* partial, const void* residual, void* out, int32_t dtype, int64_t n,
@@ -563,13 +663,14 @@ int fd_residual_add_out(const float* partial, const void* residual, void* out, i
   if (!partial || !residual || !out || n < 0 || !half_dtype(dtype)) return FD_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned blocks = stream_blocks(n, 256);
-  if (dtype == FD_BF16)
-    residual_add_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-        partial, static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), n);
-  else
-    residual_add_kernel<__half><<<blocks, 256, 0, st>>>(partial, static_cast<const __half*>(residual),
-                                                        static_cast<__half*>(out), n);
-  return from_cuda(cudaGetLastError());
+  using fd_host::launch_pdl;
+  const cudaError_t e =
+      dtype == FD_BF16
+          ? launch_pdl(residual_add_kernel<__nv_bfloat16>, blocks, 256, 0, st, partial,
+                       static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), n)
+          : launch_pdl(residual_add_kernel<__half>, blocks, 256, 0, st, partial, static_cast<const __half*>(residual),
+                       static_cast<__half*>(out), n);
+  return from_cuda(e);
 }
 
 int fd_copy(void* dst, const void* src, size_t bytes, void* stream) {

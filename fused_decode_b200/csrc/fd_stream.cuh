@@ -180,8 +180,6 @@ FD_DEV void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 FD_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS) : "memory"); }
-FD_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-FD_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Byte offset of 16-byte chunk c of row r inside a 128B-swizzled tile whose
 // rows are 128 bytes (TMA CU_TENSOR_MAP_SWIZZLE_128B, 1024-byte aligned base).
@@ -191,13 +189,6 @@ FD_DEV uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^
 FD_DEV int64_t range_start(int64_t c, int64_t total, int64_t G) { return c * total / G; }
 // The CTA whose range holds step t.
 FD_DEV int64_t cta_of(int64_t t, int64_t total, int64_t G) { return ((t + 1) * G - 1) / total; }
-
-FD_DEV float silu_mul(float g, float u) {
-  // Stable sigmoid, as the reference kernel computes it (kernels.py:448-451).
-  const float e = expf(-fabsf(g));
-  const float sig = g >= 0.f ? 1.0f / (1.0f + e) : e / (1.0f + e);
-  return g * sig * u;
-}
 
 // Accumulator ownership shared by both kinds: lane (g, q) owns, for tile t and
 // element e, weight row g + 8*(e>>1) of its warp and batch column
