@@ -71,6 +71,19 @@ SIGNATURES: dict[str, tuple] = {
             c_vp, c_size, c_vp,          # workspace, bytes, stream
         ],
     ),
+    "fd_linear_noalloc_scratch_bytes": (c_size, []),
+    "fd_linear_out_noalloc": (
+        c_i32,
+        [
+            c_vp, c_i64, c_i64,          # x, sxm, sxk
+            c_vp, c_i64, c_i64,          # w, swn, swk
+            c_vp, c_i32, c_i64,          # bias, bias_dtype, sbias
+            c_vp, c_i32, c_i64, c_i64,   # row_add, ra_dtype, srm, srn
+            c_vp, c_i64, c_i64,          # y, sym, syn
+            c_i32, c_i32, c_i64, c_i64, c_i32,  # dtype, m, n, k, kind
+            c_vp,                        # stream
+        ],
+    ),
     "fd_post_attn_mlp_workspace_bytes": (c_size, [c_i32, c_i64, c_i64]),
     "fd_post_attn_mlp_out": (
         c_i32,

@@ -6,6 +6,8 @@
 // griddepcontrol.wait, so it overlaps the previous kernel's tail.
 #include "fd_stream.cuh"
 
+#include <mutex>
+
 using namespace fd;
 using namespace fd_stream;
 
@@ -381,6 +383,63 @@ int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers, const void* c
     cur = dst;
   }
   return FD_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- no-alloc GEMV
+// fd_linear_out_noalloc runs fd_linear_out with a scratch area that lives in
+// this library's own static device memory instead of a caller workspace.  It
+// is for callers that have no device memory to hand over: a host that has no
+// allocator of its own, or one whose memory plan is frozen after start-up and
+// forbids any further device allocation.  Nothing here allocates.
+//
+// The scratch holds the same layout as a caller workspace (split-K slots,
+// per-block counters, the status word).  Static device memory is zero when
+// the library's code is loaded onto a device, which is the state the counters
+// and the status word must start in; every completed launch leaves the
+// counters at zero again.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t{6} << 20;  // 6 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Address of the current device's copy of the scratch.  Looked up once per
+// device (the first call on that device) and cached.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return FD_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return FD_ERR_DEVICE;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fd_linear_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int fd_linear_out_noalloc(const void* x, int64_t sxm, int64_t sxk, const void* w, int64_t swn, int64_t swk,
+                          const void* bias, int32_t bias_dtype, int64_t sbias, const void* row_add,
+                          int32_t ra_dtype, int64_t srm, int64_t srn, void* y, int64_t sym, int64_t syn,
+                          int32_t dtype, int32_t m, int64_t n, int64_t k, int32_t kind, void* stream) {
+  if (fd_linear_workspace_bytes(m, n, k) > kNoAllocScratchBytes) return FD_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int r = noalloc_scratch(&scratch);
+  if (r != FD_OK) return r;
+  return fd_linear_out(x, sxm, sxk, w, swn, swk, bias, bias_dtype, sbias, row_add, ra_dtype, srm, srn, y, sym, syn,
+                       dtype, m, n, k, kind, scratch, kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"

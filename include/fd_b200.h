@@ -115,6 +115,30 @@ int fd_linear_out(const void* x, int64_t sxm, int64_t sxk,
                   int32_t dtype, int32_t m, int64_t n, int64_t k, int32_t kind,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* fd_linear_out without a workspace argument.  No counterpart in the
+ * reference (its launchers allocate through PyTorch).  For callers that have
+ * no device memory to hand over -- a host without an allocator of its own, or
+ * one whose memory plan forbids device allocation after start-up -- the
+ * split-K scratch lives in the library's static device memory: at most
+ * fd_linear_noalloc_scratch_bytes() (6 MiB) per device.  Nothing is allocated.
+ *   - The first call on a device looks up that device's scratch address
+ *     (set-up, done once per device; make it before any stream capture).
+ *   - The scratch starts at zero when the library is loaded on a device, and
+ *     every completed launch leaves its counters at zero again.
+ *   - All calls on one device share the one scratch: calls that overlap in
+ *     time (concurrent streams, threads) race; serialise them.
+ *   - Returns FD_ERR_WORKSPACE when the device needs more scratch than the
+ *     built-in size (fd_linear_workspace_bytes() above it, i.e. a GPU with more
+ *     than 183 SMs); otherwise the return values of fd_linear_out. */
+size_t fd_linear_noalloc_scratch_bytes(void);
+int fd_linear_out_noalloc(const void* x, int64_t sxm, int64_t sxk,
+                          const void* w, int64_t swn, int64_t swk,
+                          const void* bias, int32_t bias_dtype, int64_t sbias,
+                          const void* row_add, int32_t ra_dtype, int64_t srm, int64_t srn,
+                          void* y, int64_t sym, int64_t syn,
+                          int32_t dtype, int32_t m, int64_t n, int64_t k, int32_t kind,
+                          void* stream);
+
 /* Workspace bytes fd_post_attn_mlp_out / fd_mlp_gate_up_out need (zero-filled
  * once, as above). */
 size_t fd_post_attn_mlp_workspace_bytes(int32_t m, int64_t h, int64_t i);
