@@ -24,20 +24,31 @@ __global__ void __launch_bounds__(MAXT, MINB)
   __shared__ int s_last;
   __shared__ int s_abort;
   __shared__ float s_sumsq[GW][MT_MAX];
+  __shared__ __align__(8) uint64_t s_mid[2];
+  __shared__ int s_mid_last;
   const int64_t xbytes = MODE == MODE_GATEUP ? static_cast<int64_t>(gateup_x_bytes(a.m, a.ks, a.boxes))
                                              : static_cast<int64_t>(a.stages) * a.boxes * a.x_slot;
   const Ring r = carve_ring(smem_raw, a.stages, a.boxes, a.x_slot, xbytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int P = static_cast<int>(blockDim.x >> 5) - GW;
+  const int P = static_cast<int>(blockDim.x >> 5) - GW - 1;  // warps: consumers, producers, announcer
   const int64_t G = gridDim.x, c = blockIdx.x;
   const int64_t s0 = range_start(c, a.total, G);
   const int64_t s1 = range_start(c + 1, a.total, G);
+  const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last};
 
   if (threadIdx.x == 0) {
-    ring_init(r);
+    mbar_init(&s_mid[0], GW);
+    mbar_init(&s_mid[1], 1);
+    ring_init(r);  // ends with the mbarrier-init fence
     s_abort = 0;
   }
   __syncthreads();
+
+  if (warp == GW + P) {
+    if (lane == 0) announce_mid(a, ms, s0, s1, G, &s_abort);
+    grid_dep_launch();
+    return;
+  }
 
   if (warp >= GW) {
     // producer warps: producer p issues ring indices p, p+P, ...
@@ -55,10 +66,12 @@ __global__ void __launch_bounds__(MAXT, MINB)
     return;
   }
   // consumer warps
+  float wv[4][8];
+  if (MODE == MODE_GATEUP) norm_weights(a, r, wv);
   grid_dep_wait();
-  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, r, s_sumsq);
+  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, r, s_sumsq, wv);
   grid_dep_launch();
-  consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort);
+  consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort, ms);
 }
 
 // ------------------------------------------------------------ generic GEMV
@@ -118,11 +131,10 @@ cudaError_t launch_tma(Kern kern, const CUtensorMap& wm, const CUtensorMap& xm, 
                        const Geometry& geo, size_t smem, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const int64_t grid =
-      std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(fd_host::sm_count()) * geo.ctas_per_sm, a.total));
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(fd_host::sm_count(), a.total));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(CONSUMERS + 32 * geo.producers);
+  cfg.blockDim = dim3(CONSUMERS + 32 * (geo.producers + 1));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -133,30 +145,15 @@ cudaError_t launch_tma(Kern kern, const CUtensorMap& wm, const CUtensorMap& xm, 
   return cudaLaunchKernelEx(&cfg, kern, wm, xm, a);
 }
 
-template <typename T, int MODE, int NT, int KIND, int MP>
-cudaError_t launch_geo(const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, const Geometry& geo,
-                       size_t smem, cudaStream_t st) {
-  if (geo.ctas_per_sm == 2)
-    return launch_tma(gemv_tma_kernel<T, NT, KIND, MP, MODE, CONSUMERS + 32, 2>, wm, xm, a, geo, smem, st);
-  return launch_tma(gemv_tma_kernel<T, NT, KIND, MP, MODE, CONSUMERS + 32 * MAX_PRODUCERS, 1>, wm, xm, a, geo,
-                    smem, st);
-}
-
 template <typename T, int MODE>
 cudaError_t dispatch_tma(const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, int kind,
                          const Geometry& geo, size_t smem, cudaStream_t st) {
+  auto L = [&](auto kern) { return launch_tma(kern, wm, xm, a, geo, smem, st); };
+  constexpr int MT1 = CONSUMERS + 32 * (MAX_PRODUCERS + 1);
   if (kind == FD_KIND_DOT) {
-    if (a.m <= 8) return launch_geo<T, MODE, 1, 0, 1>(wm, xm, a, geo, smem, st);
-    return launch_geo<T, MODE, 2, 0, 1>(wm, xm, a, geo, smem, st);
+    if (a.m <= 8) return L(gemv_tma_kernel<T, 1, 0, 1, MODE, MT1, 1>);
+    return L(gemv_tma_kernel<T, 2, 0, 1, MODE, MT1, 1>);
   }
-  // simt: one CTA per SM (its accumulators need the registers)
-  Geometry g1 = geo;
-  if (g1.ctas_per_sm == 2) {
-    g1.ctas_per_sm = 1;
-    g1.producers = 2;
-  }
-  auto L = [&](auto kern) { return launch_tma(kern, wm, xm, a, g1, smem, st); };
-  constexpr int MT1 = CONSUMERS + 32 * MAX_PRODUCERS;
   if (a.m <= 1) return L(gemv_tma_kernel<T, 1, 1, 1, MODE, MT1, 1>);
   if (a.m <= 2) return L(gemv_tma_kernel<T, 1, 1, 2, MODE, MT1, 1>);
   if (a.m <= 4) return L(gemv_tma_kernel<T, 1, 1, 4, MODE, MT1, 1>);

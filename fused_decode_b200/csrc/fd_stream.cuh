@@ -23,6 +23,10 @@
 //    to finish a block (an atomic counter) sums the slots in CTA order --
 //    deterministic, no inter-CTA waiting -- applies the epilogue and re-zeroes
 //    the counter, so the workspace is ready for the next launch or replay.
+//    A block that ends in the middle of a CTA's range is published by a
+//    separate announcer warp, so the consumer warps never stop streaming for
+//    the fence and counter round trips (measured: CTAs crossing a block
+//    boundary otherwise finished 3-4 us after the others).
 //  * Every wait is bounded (globaltimer): on expiry the CTA sets a bit in the
 //    workspace status word and leaves instead of hanging.
 #pragma once
@@ -208,10 +212,31 @@ struct Acc {
 template <typename T, int NT, int MODE>
 struct Epilogue;
 
-// Plain linear: y = round(acc + bias + row_add)  (or the fp32 sum).
+// Plain linear: y = round(acc + bias + row_add)  (or the fp32 sum).  The
+// addends are loaded by extras() -- ahead of time where the caller can, so
+// their memory round trip overlaps the split-K bookkeeping.
 template <typename T, int NT>
 struct Epilogue<T, NT, MODE_LINEAR> {
-  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* /*xchg*/) {
+  FD_DEV static void extras(const GemvArgs& a, int64_t blk, Acc<NT>& ex) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
+        const int col = 8 * t + 2 * q + (e & 1);
+        float v = 0.f;
+        if (row < a.n && col < a.m) {
+          if (a.bias) v += load_as_f32(a.bias, a.bias_dtype, row * a.sbias);
+          // row_add may have been written by an earlier kernel: read through L2
+          if (a.ra) v += load_as_f32_cg(a.ra, a.ra_dtype, col * a.srm + row * a.srn);
+        }
+        ex.v[t][e] = v;
+      }
+    }
+  }
+  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& ex, float* /*xchg*/) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
 #pragma unroll
@@ -221,10 +246,7 @@ struct Epilogue<T, NT, MODE_LINEAR> {
         const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
         const int col = 8 * t + 2 * q + (e & 1);
         if (row < a.n && col < a.m) {
-          float v = acc.v[t][e];
-          if (a.bias) v += load_as_f32(a.bias, a.bias_dtype, row * a.sbias);
-          // row_add may have been written earlier in this kernel by another CTA: read through L2
-          if (a.ra) v += load_as_f32_cg(a.ra, a.ra_dtype, col * a.srm + row * a.srn);
+          const float v = acc.v[t][e] + ex.v[t][e];
           if (a.y_f32)
             reinterpret_cast<float*>(a.y)[col * a.sym + row * a.syn] = v;
           else
@@ -240,7 +262,8 @@ struct Epilogue<T, NT, MODE_LINEAR> {
 // (reference.py:390, ops.py:313), then mid = round(silu(gate) * up).
 template <typename T, int NT>
 struct Epilogue<T, NT, MODE_GATEUP> {
-  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* xchg) {
+  FD_DEV static void extras(const GemvArgs&, int64_t, Acc<NT>& ex) { ex.zero(); }
+  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& /*ex*/, float* xchg) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
     constexpr int HALF = GW / 2;
@@ -274,20 +297,18 @@ struct Epilogue<T, NT, MODE_GATEUP> {
   }
 };
 
-// Block `blk` ends inside this CTA's range [s0, s1): finish it directly if the
-// CTA covered all of it, else publish the partial and let the last of the
-// block's CTAs reduce.  Called by all consumer threads together.
-template <typename T, int NT, int MODE>
-FD_DEV void flush_block(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, float* xchg, int64_t s0, int64_t s1,
-                        int64_t G, int64_t c, int* s_last) {
+// Split-K bookkeeping.  A CTA's range [s0, s1) holds at most two blocks it
+// does not cover whole: the block it starts inside (slot 0) and the block it
+// ends inside (slot 1).  Their partials go to the CTA's two slots with plain
+// stores as soon as each is finished; both are announced together at the end
+// of the range (settle), so finishing the first one never stalls the weight
+// stream.  Every block's last-arriving contributor sums the slots of all its
+// contributors in CTA order -- the result does not depend on timing -- applies
+// the epilogue and re-zeroes the block's counter.
+template <int NT>
+FD_DEV void write_slot(const GemvArgs& a, int slot, const Acc<NT>& acc, int64_t c) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
-  const bool covered = (s0 <= blk * a.ks) && (s1 >= (blk + 1) * a.ks);
-  if (covered) {
-    Epilogue<T, NT, MODE>::run(a, blk, acc, xchg);
-    return;
-  }
-  const int slot = (blk == s0 / a.ks) ? 0 : 1;
   float* sp = a.slots + (c * 2 + slot) * (BR * MT_MAX);
 #pragma unroll
   for (int t = 0; t < NT; ++t)
@@ -297,51 +318,104 @@ FD_DEV void flush_block(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, floa
       const int col = 8 * t + 2 * q;
       *reinterpret_cast<float2*>(sp + r * MT_MAX + col) = make_float2(acc.v[t][2 * h], acc.v[t][2 * h + 1]);
     }
-  __threadfence();
-  consumer_sync();
+}
+
+// Sum block blk's partials (every contributor's slot, in CTA order) and run
+// the epilogue with the addends `ex`.  Called by all consumer threads of the
+// CTA that completes the block.
+template <typename T, int NT, int MODE>
+FD_DEV void reduce_block(const GemvArgs& a, int64_t blk, float* xchg, int64_t G, const Acc<NT>& ex) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
   const int64_t cf = cta_of(blk * a.ks, a.total, G);
   const int64_t cl = cta_of((blk + 1) * a.ks - 1, a.total, G);
+  Acc<NT> sum;
+  sum.zero();
+  // Contributors' slots are loaded UNROLL at a time, all in flight together
+  // (one L2 round trip per batch, not one per slot), then added in CTA order.
+  constexpr int UNROLL = 8;
+  for (int64_t c0 = cf; c0 <= cl; c0 += UNROLL) {
+    float2 v[UNROLL][NT][2];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t cc = c0 + u;
+      const int sl = (cc <= cl && blk != range_start(cc, a.total, G) / a.ks) ? 1 : 0;
+      const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          v[u][t][h] = cc <= cl ? __ldcg(reinterpret_cast<const float2*>(rp + (16 * warp + g + 8 * h) * MT_MAX +
+                                                                         8 * t + 2 * q))
+                                : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          sum.v[t][2 * h] += v[u][t][h].x;
+          sum.v[t][2 * h + 1] += v[u][t][h].y;
+        }
+  }
+  Epilogue<T, NT, MODE>::run(a, blk, sum, ex, xchg);
+  if (threadIdx.x == 0) a.counters[blk] = 0;
+}
+
+// Publish the partial of block blk (already in this CTA's slot) and, if this
+// CTA is the block's last contributor, reduce it.  All consumer threads.
+template <typename T, int NT, int MODE>
+FD_DEV void settle(const GemvArgs& a, int64_t blk, float* xchg, int64_t G, int* s_last) {
+  Acc<NT> ex;
+  Epilogue<T, NT, MODE>::extras(a, blk, ex);  // in flight during the bookkeeping below
+  __threadfence();  // this thread's slot stores are visible device-wide ...
+  consumer_sync();  // ... for every consumer thread, before the count below
   if (threadIdx.x == 0) {
-    const int old = atomicAdd(a.counters + blk, 1);
-    *s_last = (old == static_cast<int>(cl - cf));
+    const int64_t cf = cta_of(blk * a.ks, a.total, G);
+    const int64_t cl = cta_of((blk + 1) * a.ks - 1, a.total, G);
+    *s_last = atomicAdd(a.counters + blk, 1) == static_cast<int>(cl - cf);
   }
   consumer_sync();
   if (*s_last) {
     __threadfence();
-    Acc<NT> sum;
-    sum.zero();
-    // Contributors' slots are loaded UNROLL at a time, all in flight together
-    // (one L2 round trip per batch under full HBM load, not one per slot), then
-    // added in CTA order so the result does not depend on timing.
-    constexpr int UNROLL = 4;
-    for (int64_t c0 = cf; c0 <= cl; c0 += UNROLL) {
-      float2 v[UNROLL][NT][2];
-#pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        const int64_t cc = c0 + u;
-        const int sl = (cc <= cl && blk != range_start(cc, a.total, G) / a.ks) ? 1 : 0;
-        const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            v[u][t][h] = cc <= cl ? __ldcg(reinterpret_cast<const float2*>(rp + (16 * warp + g + 8 * h) * MT_MAX +
-                                                                           8 * t + 2 * q))
-                                  : make_float2(0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            sum.v[t][2 * h] += v[u][t][h].x;
-            sum.v[t][2 * h + 1] += v[u][t][h].y;
-          }
-    }
-    Epilogue<T, NT, MODE>::run(a, blk, sum, xchg);
-    if (threadIdx.x == 0) a.counters[blk] = 0;
+    reduce_block<T, NT, MODE>(a, blk, xchg, G, ex);
   }
+}
+
+
+// The first block of a CTA's range, when the CTA does not cover all of it and
+// the block ends before the range does, is finished mid-stream.  Its partial
+// is written to slot 0 and published by a separate announcer warp (fence +
+// counter), so the consumer warps go on streaming instead of waiting through
+// those memory round trips; if the announcer finds this CTA completed the
+// block, the consumers reduce it at the end of their range.
+struct MidSync {
+  uint64_t* ready;  // consumer warps -> announcer: slot 0 written (count GW)
+  uint64_t* done;   // announcer -> consumers: published, *last valid (count 1)
+  int* last;
+};
+
+FD_DEV bool has_mid_block(int64_t s0, int64_t s1, int64_t ks) { return s0 % ks != 0 && (s0 / ks + 1) * ks < s1; }
+
+// Lane 0 of the announcer warp.
+FD_DEV void announce_mid(const GemvArgs& a, const MidSync& ms, int64_t s0, int64_t s1, int64_t G, int* s_abort) {
+  if (!has_mid_block(s0, s1, a.ks)) return;
+  const int64_t b0 = s0 / a.ks;
+  int last = 0;
+  if (mbar_wait(ms.ready, 0)) {
+    if (!*reinterpret_cast<volatile int*>(s_abort)) {
+      __threadfence();  // the consumers' slot stores (ordered before the mbarrier) first
+      const int64_t cf = cta_of(b0 * a.ks, a.total, G);
+      const int64_t cl = cta_of((b0 + 1) * a.ks - 1, a.total, G);
+      last = atomicAdd(a.counters + b0, 1) == static_cast<int>(cl - cf);
+    }
+  } else {
+    atomicOr(a.status, kStatusFullTimeout);
+    *s_abort = 1;
+  }
+  *ms.last = last;
+  mbar_arrive(ms.done);
 }
 
 // ------------------------------------------------------------ the ring
@@ -472,9 +546,28 @@ FD_DEV void producer_drain(const Ring& r, int64_t end, int p, int P) {
 // groups whose loads (hidden and norm weight) are all issued at once: one
 // round trip per group -- a single group for m * k <= 8 * 256 * 8 (k <= 8192
 // here; wider rows take two passes).
-// Called by all consumer threads; ends with a consumer barrier.
+// norm_to_smem is called by all consumer threads and ends with a consumer
+// barrier; its norm-weight operands come from norm_weights().
+//
+// The norm weight elements this consumer thread scales (rows of up to
+// 4 x 256 vectors of 8).  They do not depend on the previous kernel, so the
+// kernel loads them before griddepcontrol.wait.
+FD_DEV void norm_weights(const GemvArgs& a, const Ring& r, float (&wv)[4][8]) {
+  const int tid = threadIdx.x;
+  const int nvec = static_cast<int>(a.k / 8);
+  const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
+  const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;
+  const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int v = tid + j * CONSUMERS;
+    if (jv <= 4 && j < jv && v < nvec)
+      load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv[j]);
+  }
+}
+
 template <typename T>
-FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]) {
+FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const float (&wv)[4][8]) {
   constexpr int REGS = 8;  // 16-byte vectors of hidden held per thread per group
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned char* xs = r.xreg;
@@ -487,7 +580,6 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
     for (int r0 = 0; r0 < a.m; r0 += rows_per_group) {
       const int nr = min(rows_per_group, a.m - r0);
       uint4 hv[REGS];
-      float wv[4][8];
       // issue every load of the group first
 #pragma unroll
       for (int e = 0; e < REGS; ++e) {
@@ -497,12 +589,6 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
         if (rr < nr && v < nvec)
           hv[e] = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) +
                                                          (r0 + rr) * a.hidden_stride) + v);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int v = tid + j * CONSUMERS;
-        if (j < jv && v < nvec)
-          load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv[j]);
       }
       float ss[REGS];
 #pragma unroll
@@ -595,7 +681,7 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
 // base ..; flushes every finished block.  Returns false when a wait expired.
 template <typename T, int NT, int KIND, int MP, int MODE>
 FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t s1, int64_t base, int64_t G,
-                          int64_t c, int* s_last, int* s_abort) {
+                          int64_t c, int* s_last, int* s_abort, const MidSync& ms) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int B = r.B;
@@ -720,7 +806,20 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
             acc.v[t][e] = v;
           }
       }
-      flush_block<T, NT, MODE>(a, cb, acc, r.xchg, s0, s1, G, c, s_last);
+      const bool covered = (s0 <= cb * a.ks) && (s1 >= (cb + 1) * a.ks);
+      if (covered) {
+        Acc<NT> ex;
+        Epilogue<T, NT, MODE>::extras(a, cb, ex);
+        Epilogue<T, NT, MODE>::run(a, cb, acc, ex, r.xchg);
+      } else if (it + 1 < s1 - s0) {
+        // the range's first block ends mid-stream: hand it to the announcer
+        write_slot<NT>(a, 0, acc, c);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ms.ready);
+      } else {
+        write_slot<NT>(a, cb == s0 / a.ks ? 0 : 1, acc, c);
+        settle<T, NT, MODE>(a, cb, r.xchg, G, s_last);
+      }
       acc.zero();
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr)
@@ -730,13 +829,26 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
       ++cb;
     }
   }
+  if (has_mid_block(s0, s1, a.ks)) {
+    if (!mbar_wait(ms.done, 0)) {
+      atomicOr(a.status, kStatusFullTimeout);
+      *s_abort = 1;
+      return false;
+    }
+    if (*ms.last) {
+      Acc<NT> ex;
+      Epilogue<T, NT, MODE>::extras(a, s0 / a.ks, ex);
+      __threadfence();
+      reduce_block<T, NT, MODE>(a, s0 / a.ks, r.xchg, G, ex);
+    }
+  }
   return true;
 }
 
 // ------------------------------------------------------------ host side
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-constexpr int kMaxCtasPerSm = 2;
+constexpr int kMaxCtasPerSm = 2;  // workspace slots are sized for up to two CTAs per SM
 inline int64_t max_grid() { return static_cast<int64_t>(fd_host::sm_count()) * kMaxCtasPerSm; }
 
 // Workspace layout (fixed for a device, whatever the shape, so one buffer can
@@ -820,38 +932,28 @@ inline size_t ring_smem_bytes(size_t xbytes, int stages, int boxes) {
 constexpr size_t kSmemPerSm = 228 * 1024;          // shared memory of one SM
 constexpr size_t kSmemPerCta = 227 * 1024 - 1024;  // opt-in maximum, less static shared memory
 
-// Pipeline geometry of one launch: CTAs per SM, producer warps, 64-column
-// boxes per step and ring stages.  Measured on B200 over the Llama-3-8B MLP
-// shapes (32-launch CUDA graphs, M = 1 and 8): one CTA per SM with two
-// producer warps, 32 KB steps (two boxes) and four stages streamed fastest
-// (gate/up 5.0 TB/s, down 4.5 TB/s); two CTAs per SM with one producer each
-// were 3-10% slower, 16 KB steps 20-30% slower.  `xbytes(stages, boxes)`
-// gives the X region the kernel needs.
+// Pipeline geometry of one launch: producer warps, 64-column boxes per step
+// and ring stages (one CTA per SM).  Measured on B200 over the Llama-3-8B MLP
+// shapes (32-launch CUDA graphs, M = 1 and 8): two producer warps, 32 KB
+// steps (two boxes) and four stages streamed fastest; 16 KB steps were 20-30 %
+// slower, two CTAs per SM with one producer each 3-10 % slower.
+// `xbytes(stages, boxes)` gives the X region the kernel needs.
 struct Geometry {
-  int ctas_per_sm, producers, boxes, stages;
+  int producers, boxes, stages;
 };
 
 template <typename XBytes>
 Geometry choose_geometry(XBytes xbytes) {
-  Geometry g{1, 2, 2, 4};
-  if (const char* env = std::getenv("FD_GEMV_GEOMETRY")) {  // tuning override: "cps,producers,boxes,stages"
-    int a = 0, b = 0, c = 0, d = 0;
-    if (std::sscanf(env, "%d,%d,%d,%d", &a, &b, &c, &d) == 4 && a >= 1 && a <= 2 && b >= 1 && b <= MAX_PRODUCERS &&
-        c >= 1 && c <= MAX_BOXES && d >= 2 && d <= MAX_STAGES)
-      g = {a, b, c, d};
+  Geometry g{2, 2, 4};
+  if (const char* env = std::getenv("FD_GEMV_GEOMETRY")) {  // tuning override: "producers,boxes,stages"
+    int b = 0, c = 0, d = 0;
+    if (std::sscanf(env, "%d,%d,%d", &b, &c, &d) == 3 && b >= 1 && b <= MAX_PRODUCERS && c >= 1 &&
+        c <= MAX_BOXES && d >= 2 && d <= MAX_STAGES)
+      g = {b, c, d};
   }
-  const size_t per_cta = g.ctas_per_sm == 2 ? kSmemPerSm / 2 - 2048 : kSmemPerCta;
   auto bytes = [&](int st) { return ring_smem_bytes(xbytes(st, g.boxes), st, g.boxes); };
-  while (g.stages > 2 && bytes(g.stages) > per_cta) --g.stages;
-  if (bytes(g.stages) > per_cta && g.ctas_per_sm == 2) {
-    // Two CTAs do not fit (a wide normalised batch): one CTA, two producers.
-    g.ctas_per_sm = 1;
-    g.producers = std::max(g.producers, 2);
-    g.stages = MAX_STAGES;
-    while (g.stages > 2 && bytes(g.stages) > kSmemPerCta) --g.stages;
-  }
-  if (g.ctas_per_sm == 2) g.producers = 1;  // the two-CTA kernels are built for 288 threads
-  g.stages -= g.stages % g.producers;       // every stage is always refilled by the same producer
+  while (g.stages > 2 && bytes(g.stages) > kSmemPerCta) --g.stages;
+  g.stages -= g.stages % g.producers;  // every stage is always refilled by the same producer
   if (g.stages < 2 || bytes(g.stages) > kSmemPerCta) g.stages = 0;
   return g;
 }
