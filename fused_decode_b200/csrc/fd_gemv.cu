@@ -25,8 +25,10 @@ __global__ void __launch_bounds__(MAXT, MINB)
   __shared__ int s_abort;
   __shared__ float s_sumsq[GW][MT_MAX];
   __shared__ __align__(8) uint64_t s_mid[2];
-  __shared__ int s_mid_last;
-  const int64_t xbytes = MODE == MODE_GATEUP ? static_cast<int64_t>(gateup_x_bytes(a.m, a.ks, a.boxes))
+  __shared__ __align__(8) uint64_t s_nw_bar;  // norm weight copy landed (GATEUP)
+  __shared__ int s_mid_last, s_fast, s_decided;
+  const int nes = a.norm_dtype == FD_F32 ? 4 : 2;
+  const int64_t xbytes = MODE == MODE_GATEUP ? static_cast<int64_t>(gateup_region_bytes(a.m, a.ks, a.boxes, a.k, nes))
                                              : static_cast<int64_t>(a.stages) * a.boxes * a.x_slot;
   const Ring r = carve_ring(smem_raw, a.stages, a.boxes, a.x_slot, xbytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -34,18 +36,25 @@ __global__ void __launch_bounds__(MAXT, MINB)
   const int64_t G = gridDim.x, c = blockIdx.x;
   const int64_t s0 = range_start(c, a.total, G);
   const int64_t s1 = range_start(c + 1, a.total, G);
-  const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last};
+  const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided};
+  unsigned char* nw_smem = r.xreg + gateup_x_bytes(a.m, a.ks, a.boxes);  // GATEUP: norm weight copy
 
   if (threadIdx.x == 0) {
     mbar_init(&s_mid[0], GW);
     mbar_init(&s_mid[1], 1);
+    mbar_init(&s_nw_bar, 1);
     ring_init(r);  // ends with the mbarrier-init fence
     s_abort = 0;
+    s_fast = 0;
+    s_decided = 0;
   }
   __syncthreads();
 
   if (warp == GW + P) {
-    if (lane == 0) announce_mid(a, ms, s0, s1, G, &s_abort);
+    if (lane == 0) {
+      announce_mid(a, ms, s0, s1, G, &s_abort);
+      if (MODE == MODE_GATEUP) watch_final(a, ms, s0, s1, G, c);
+    }
     grid_dep_launch();
     return;
   }
@@ -54,6 +63,12 @@ __global__ void __launch_bounds__(MAXT, MINB)
     // producer warps: producer p issues ring indices p, p+P, ...
     const int p = warp - GW;
     if (lane == 0) {
+      if (MODE == MODE_GATEUP && p == 0) {
+        // the norm weight is an input, not the previous kernel's output: copy it now
+        const uint32_t nb = static_cast<uint32_t>(a.k * nes);
+        mbar_expect_tx(&s_nw_bar, nb);
+        bulk_load(nw_smem, a.norm_w, nb, &s_nw_bar);
+      }
       prefetch_map(&wmap);
       if (MODE == MODE_LINEAR) prefetch_map(&xmap);
       produce_phase<MODE>(r, &wmap, &xmap, a, s0, s1, 0, p, P, evict_first_policy(), &s_abort, [] {
@@ -66,10 +81,8 @@ __global__ void __launch_bounds__(MAXT, MINB)
     return;
   }
   // consumer warps
-  float wv[4][8];
-  if (MODE == MODE_GATEUP) norm_weights(a, r, wv);
   grid_dep_wait();
-  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, r, s_sumsq, wv);
+  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, r, s_sumsq, nw_smem, &s_nw_bar);
   grid_dep_launch();
   consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort, ms);
 }
@@ -190,9 +203,10 @@ int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvAr
 int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
                    int64_t s_gu, void* mid, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
                    const Workspace& ws, cudaStream_t st) {
-  const Geometry geo = choose_geometry([m, h](int, int boxes) {
+  const int nes = norm_dtype == FD_F32 ? 4 : 2;
+  const Geometry geo = choose_geometry([m, h, nes](int, int boxes) {
     const int64_t ks = (h + static_cast<int64_t>(boxes) * KC - 1) / (static_cast<int64_t>(boxes) * KC);
-    return gateup_x_bytes(m, ks, boxes);
+    return gateup_region_bytes(m, ks, boxes, h, nes);
   });
   if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
   GemvArgs a = {};
@@ -210,7 +224,7 @@ int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, c
   a.norm_w = norm_w; a.norm_dtype = norm_dtype; a.eps = eps;
   CUtensorMap gm;
   if (!make_gate_up_map(&gm, w_gate_up, h, i, s_gu)) return FD_ERR_LAUNCH;
-  const size_t smem = ring_smem_bytes(gateup_x_bytes(m, a.ks, a.boxes), a.stages, a.boxes);
+  const size_t smem = ring_smem_bytes(gateup_region_bytes(m, a.ks, a.boxes, h, nes), a.stages, a.boxes);
   cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st)
                                    : dispatch_tma<__half, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st);
   return from_cuda(e);

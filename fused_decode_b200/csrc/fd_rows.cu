@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(512) rms_vec_kernel(RmsArgs a) {
     sumsq = tot;
   }
   if (!live) return;
-  const float inv = 1.0f / sqrtf(sumsq / static_cast<float>(a.n) + a.eps);
+  const float inv = rsqrtf(sumsq / static_cast<float>(a.n) + a.eps);  // rsqrt, as the reference
   T* yr = reinterpret_cast<T*>(a.y.ptr) + offset_of(a.y, ri);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(256) rms_generic_kernel(RmsGenArgs a) {
   __syncthreads();
   float tot = 0.f;
   for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += red[w];
-  const float inv = 1.0f / sqrtf(tot / static_cast<float>(a.n) + a.eps);
+  const float inv = rsqrtf(tot / static_cast<float>(a.n) + a.eps);
   T* yr = row_ptr<T>(a.y, row, a.B, a.C);
   T* ror = a.store_res ? row_ptr<T>(a.ro, row, a.B, a.C) : nullptr;
   for (int64_t j = threadIdx.x; j < a.n; j += blockDim.x) {

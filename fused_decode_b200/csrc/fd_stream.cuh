@@ -117,6 +117,10 @@ FD_DEV void mma16816<__half>(float* c, uint32_t a0, uint32_t a1, uint32_t a2, ui
 }
 
 FD_DEV uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+FD_DEV void st_shared16(void* p, const uint4& v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_addr(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
 FD_DEV uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -179,6 +183,20 @@ FD_DEV void tma_load_2d_plain(void* dst, const CUtensorMap* map, int32_t x, int3
       "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`
+// (both addresses 16-byte aligned, bytes a multiple of 16).
+FD_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+FD_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 FD_DEV void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -322,9 +340,12 @@ FD_DEV void write_slot(const GemvArgs& a, int slot, const Acc<NT>& acc, int64_t 
 
 // Sum block blk's partials (every contributor's slot, in CTA order) and run
 // the epilogue with the addends `ex`.  Called by all consumer threads of the
-// CTA that completes the block.
+// CTA that completes the block.  `own`, when given, is contributor `self`'s
+// partial still in registers (its slot was never written); the sum is the
+// same either way.
 template <typename T, int NT, int MODE>
-FD_DEV void reduce_block(const GemvArgs& a, int64_t blk, float* xchg, int64_t G, const Acc<NT>& ex) {
+FD_DEV void reduce_block(const GemvArgs& a, int64_t blk, float* xchg, int64_t G, const Acc<NT>& ex,
+                         const Acc<NT>* own = nullptr, int64_t self = -1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t cf = cta_of(blk * a.ks, a.total, G);
@@ -339,15 +360,17 @@ FD_DEV void reduce_block(const GemvArgs& a, int64_t blk, float* xchg, int64_t G,
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int64_t cc = c0 + u;
+      const bool mine = own != nullptr && cc == self;
       const int sl = (cc <= cl && blk != range_start(cc, a.total, G) / a.ks) ? 1 : 0;
       const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          v[u][t][h] = cc <= cl ? __ldcg(reinterpret_cast<const float2*>(rp + (16 * warp + g + 8 * h) * MT_MAX +
-                                                                         8 * t + 2 * q))
-                                : make_float2(0.f, 0.f);
+          v[u][t][h] = mine ? make_float2(own->v[t][2 * h], own->v[t][2 * h + 1])
+                       : cc <= cl ? __ldcg(reinterpret_cast<const float2*>(rp + (16 * warp + g + 8 * h) * MT_MAX +
+                                                                            8 * t + 2 * q))
+                                  : make_float2(0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u)
@@ -394,7 +417,35 @@ struct MidSync {
   uint64_t* ready;  // consumer warps -> announcer: slot 0 written (count GW)
   uint64_t* done;   // announcer -> consumers: published, *last valid (count 1)
   int* last;
+  int* fast;        // announcer -> consumers: every other contributor of the final block has published
+  int* decided;     // consumers -> announcer: the final block's path is chosen, stop watching
 };
+
+// This CTA holds the first step of its final block but not the whole block:
+// the other contributors (later CTAs) process their parts at the start of
+// their ranges, so they have usually published before this CTA gets there.
+FD_DEV bool head_of_final(int64_t s0, int64_t s1, int64_t ks) {
+  const int64_t bf = (s1 - 1) / ks;
+  return s0 <= bf * ks && s1 < (bf + 1) * ks;
+}
+
+// Lane 0 of the announcer warp: watch the final block's count until every
+// other contributor has published (then tell the consumers they may finish
+// the block straight from their registers) or the consumers have decided.
+FD_DEV void watch_final(const GemvArgs& a, const MidSync& ms, int64_t s0, int64_t s1, int64_t G, int64_t c) {
+  if (!head_of_final(s0, s1, a.ks)) return;
+  const int64_t bf = (s1 - 1) / a.ks;
+  const int others = static_cast<int>(cta_of((bf + 1) * a.ks - 1, a.total, G) - c);
+  const uint64_t t0 = globaltimer();
+  while (!*reinterpret_cast<volatile int*>(ms.decided)) {
+    if (ld_acquire_gpu(a.counters + bf) == others) {
+      *reinterpret_cast<volatile int*>(ms.fast) = 1;
+      return;
+    }
+    if (globaltimer() - t0 > kWaitNs) return;
+    __nanosleep(1000);  // a light poll: the answer is only needed at the end of the range
+  }
+}
 
 FD_DEV bool has_mid_block(int64_t s0, int64_t s1, int64_t ks) { return s0 % ks != 0 && (s0 / ks + 1) * ks < s1; }
 
@@ -547,27 +598,23 @@ FD_DEV void producer_drain(const Ring& r, int64_t end, int p, int P) {
 // round trip per group -- a single group for m * k <= 8 * 256 * 8 (k <= 8192
 // here; wider rows take two passes).
 // norm_to_smem is called by all consumer threads and ends with a consumer
-// barrier; its norm-weight operands come from norm_weights().
-//
-// The norm weight elements this consumer thread scales (rows of up to
-// 4 x 256 vectors of 8).  They do not depend on the previous kernel, so the
-// kernel loads them before griddepcontrol.wait.
-FD_DEV void norm_weights(const GemvArgs& a, const Ring& r, float (&wv)[4][8]) {
-  const int tid = threadIdx.x;
-  const int nvec = static_cast<int>(a.k / 8);
-  const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
-  const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;
-  const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int v = tid + j * CONSUMERS;
-    if (jv <= 4 && j < jv && v < nvec)
-      load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv[j]);
+// barrier.  The norm weight (k elements of norm_dtype) is in shared memory at
+// `nw`, copied there by a bulk TMA load at kernel start that completes on `nw_bar`.
+FD_DEV void load8_smem_as_f32(const unsigned char* p, int dtype, float* f) {
+  if (dtype == FD_F32) {
+    const float4 lo = *reinterpret_cast<const float4*>(p), hi = *reinterpret_cast<const float4*>(p + 16);
+    f[0] = lo.x; f[1] = lo.y; f[2] = lo.z; f[3] = lo.w;
+    f[4] = hi.x; f[5] = hi.y; f[6] = hi.z; f[7] = hi.w;
+  } else if (dtype == FD_BF16) {
+    unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(p), f);
+  } else {
+    unpack8<__half>(*reinterpret_cast<const uint4*>(p), f);
   }
 }
 
 template <typename T>
-FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const float (&wv)[4][8]) {
+FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
+                         uint64_t* nw_bar) {
   constexpr int REGS = 8;  // 16-byte vectors of hidden held per thread per group
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned char* xs = r.xreg;
@@ -613,6 +660,7 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
         }
       }
       consumer_sync();
+      if (r0 == 0 && !mbar_wait(nw_bar, 0)) atomicOr(a.status, kStatusFullTimeout);
 #pragma unroll
       for (int e = 0; e < REGS; ++e) {
         const int rr = e / jv, j = e - (e / jv) * jv;
@@ -621,21 +669,18 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
           float tot = 0.f;
 #pragma unroll
           for (int w = 0; w < GW; ++w) tot += s_sumsq[w][rr];
-          const float inv = 1.0f / sqrtf(tot / static_cast<float>(a.k) + a.eps);
+          const float inv = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
           uint4 packed = make_uint4(0, 0, 0, 0);
           if (v < nvec) {
-            float f[8], o[8];
+            float f[8], w[8], o[8];
             unpack8<T>(hv[e], f);
+            load8_smem_as_f32(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, w);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float w = j == 0 ? wv[0][q] : j == 1 ? wv[1][q] : j == 2 ? wv[2][q] : wv[3][q];
-              o[q] = f[q] * inv * w;
-            }
+            for (int q = 0; q < 8; ++q) o[q] = f[q] * inv * w[q];
             packed = pack8<T>(o);
           }
           const int mrow = r0 + rr, chunk = v >> 3, cc = v & 7;
-          *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 +
-                                    ((cc ^ (mrow & 7)) << 4)) = packed;
+          st_shared16(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4), packed);
         }
       }
       consumer_sync();  // s_sumsq is reused by the next group
@@ -658,20 +703,20 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
     float tot = 0.f;
 #pragma unroll
     for (int w = 0; w < GW; ++w) tot += s_sumsq[w][0];
-    const float inv = 1.0f / sqrtf(tot / static_cast<float>(a.k) + a.eps);
+    const float inv = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
+    if (mrow == 0 && !mbar_wait(nw_bar, 0)) atomicOr(a.status, kStatusFullTimeout);
     for (int v = tid; v < nvec_pad; v += CONSUMERS) {
       uint4 packed = make_uint4(0, 0, 0, 0);
       if (v < nvec) {
         float f[8], wv[8], o[8];
         unpack8<T>(__ldcg(hr + v), f);
-        load8_as_f32(static_cast<const char*>(a.norm_w) + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
+        load8_smem_as_f32(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
 #pragma unroll
         for (int q = 0; q < 8; ++q) o[q] = f[q] * inv * wv[q];
         packed = pack8<T>(o);
       }
       const int chunk = v >> 3, cc = v & 7;
-      *reinterpret_cast<uint4*>(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4)) =
-          packed;
+      st_shared16(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4), packed);
     }
     consumer_sync();
   }
@@ -816,6 +861,23 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
         write_slot<NT>(a, 0, acc, c);
         __syncwarp();
         if (lane == 0) mbar_arrive(ms.ready);
+      } else if (MODE == MODE_GATEUP && head_of_final(s0, s1, a.ks)) {
+        Acc<NT> ex;
+        Epilogue<T, NT, MODE>::extras(a, cb, ex);
+        if (threadIdx.x == 0) {
+          *s_last = *reinterpret_cast<volatile int*>(ms.fast);
+          *reinterpret_cast<volatile int*>(ms.decided) = 1;
+        }
+        consumer_sync();
+        if (*s_last) {
+          // every other contributor has published: this CTA completes the
+          // block without publishing its own partial
+          __threadfence();
+          reduce_block<T, NT, MODE>(a, cb, r.xchg, G, ex, &acc, c);
+        } else {
+          write_slot<NT>(a, cb == s0 / a.ks ? 0 : 1, acc, c);
+          settle<T, NT, MODE>(a, cb, r.xchg, G, s_last);
+        }
       } else {
         write_slot<NT>(a, cb == s0 / a.ks ? 0 : 1, acc, c);
         settle<T, NT, MODE>(a, cb, r.xchg, G, s_last);
@@ -920,6 +982,10 @@ __host__ __device__ inline int x_slot_bytes(int m) { return m <= 8 ? 1024 : 2048
 
 __host__ __device__ inline size_t gateup_x_bytes(int m, int64_t ks, int boxes) {
   return static_cast<size_t>(ks) * boxes * m * 128;
+}
+// The gate/up X region: the normalised batch, then the norm weight's copy.
+__host__ __device__ inline size_t gateup_region_bytes(int m, int64_t ks, int boxes, int64_t k, int norm_es) {
+  return gateup_x_bytes(m, ks, boxes) + ((static_cast<size_t>(k) * norm_es + 15) & ~static_cast<size_t>(15));
 }
 __host__ __device__ inline size_t linear_x_bytes(int m, int stages, int boxes) {
   return static_cast<size_t>(stages) * boxes * x_slot_bytes(m);

@@ -286,8 +286,14 @@ def mlp_fusable(hidden2: torch.Tensor, norm_weight: torch.Tensor, w_gate_up: tor
     for t in (hidden2, norm_weight, w_gate_up, w_down):
         if t.data_ptr() % 16:
             return False
-    # RMSNorm'd batch kept in shared memory: m rows of h (+32) 2-byte elements.
-    return m * (h + 32) * 2 + 64 * 16 * 4 <= 200 * 1024
+    # Shared memory of the gate/up kernel with its smallest ring (2 stages of
+    # 32 KB): the RMSNorm'd batch (h padded to 128 columns) and a copy of the
+    # norm weight (fd_stream.cuh: ring_smem_bytes, gateup_region_bytes).
+    ks = -(-h // 128)
+    nes = 4 if norm_weight.dtype == torch.float32 else 2
+    region = ks * 2 * m * 128 + ((h * nes + 15) & ~15)
+    smem = 1024 + 2 * 32768 + region + 64 * 16 * 4 + 2 * 12 * 8
+    return smem <= 227 * 1024 - 1024
 
 
 def post_attn_mlp_out(
