@@ -118,3 +118,61 @@ def test_tp_nccl_layers():
         x = x0 if x is None else x
         x = O.post_attn_mlp(x, nw, wgu, wd, EPS, "bfloat16")
     torch.testing.assert_close(torch.from_numpy(outs[0]), torch.from_numpy(x), **TOL)
+
+
+def _rope_tables(positions, dim, theta=500000.0):
+    inv = theta ** (-torch.arange(0, dim, 2, dtype=torch.float32) / dim)
+    f = torch.outer(torch.arange(positions, dtype=torch.float32), inv)
+    emb = torch.cat((f, f), dim=-1)
+    return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m", [1, 4, 8])
+def test_tp_decode_block_llama70b(m):
+    """BASELINE config 5 at full Llama-3-70B widths (hidden 8192, intermediate
+    28672, 64 query / 8 KV heads of 128): add_rms_norm, RoPE on q and k, then
+    the MLP with gate/up column-sharded and down row-sharded over 8 emulated
+    ranks on one GPU (the allreduce is the fp32 sum of the rank partials), then
+    the residual add.  Every stage against the oracle at atol = rtol = 1e-2."""
+    from fused_decode_b200 import add_rms_norm, rope
+
+    h, i, world, eps = 8192, 28672, 8, 1e-5
+    g = torch.Generator(device="cpu").manual_seed(70 + m)
+    bf = torch.bfloat16
+    x = torch.randn(m, h, generator=g).to(bf).cuda()
+    res = torch.randn(m, h, generator=g).to(bf).cuda()
+    attn_w = (1 + 0.1 * torch.randn(h, generator=g)).to(bf).cuda()
+    q = torch.randn(m, 1, 64, 128, generator=g).to(bf).cuda()
+    k = torch.randn(m, 1, 8, 128, generator=g).to(bf).cuda()
+    cos, sin = _rope_tables(1024, 128)
+    pos = torch.randint(0, 1024, (m,), generator=g)
+    cos_b = cos[pos].view(m, 1, 1, 128).cuda()
+    sin_b = sin[pos].view(m, 1, 1, 128).cuda()
+    # random-init layer weights, N(0, 0.02)
+    mlp_w = (1 + 0.1 * torch.randn(h, generator=g)).to(bf).cuda()
+    wgu = torch.empty(2 * i, h, dtype=bf, device="cuda")
+    wd = torch.empty(h, i, dtype=bf, device="cuda")
+    gd = torch.Generator(device="cuda").manual_seed(700 + m)
+    for r0 in range(0, 2 * i, 8192):  # chunked to bound the fp32 temporary
+        wgu[r0:r0 + 8192] = (torch.randn(min(8192, 2 * i - r0), h, device="cuda", generator=gd) * 0.02).to(bf)
+    for r0 in range(0, h, 2048):
+        wd[r0:r0 + 2048] = (torch.randn(2048, i, device="cuda", generator=gd) * 0.02).to(bf)
+
+    # stage 1: add_rms_norm (attention-out residual) and RoPE on q/k
+    normed, hidden = add_rms_norm(x, res, attn_w, eps)
+    ref_normed, ref_hidden = O.add_rms_norm(_np(x), _np(res), _np(attn_w), eps, "bfloat16")
+    torch.testing.assert_close(normed.float().cpu(), torch.from_numpy(ref_normed), **TOL)
+    torch.testing.assert_close(hidden.float().cpu(), torch.from_numpy(ref_hidden), **TOL)
+    for t in (q, k):
+        out = rope(t, cos_b, sin_b)
+        ref = O.rope(_np(t), _np(cos_b), _np(sin_b), "bfloat16")
+        torch.testing.assert_close(out.float().cpu(), torch.from_numpy(ref), **TOL)
+
+    # stage 2: tensor-parallel MLP, ranks emulated in order on one GPU
+    total = torch.zeros(m, h, device="cuda", dtype=torch.float32)
+    for r in range(world):
+        mod = tp.TPPostAttnMlp.from_full(mlp_w, wgu, wd, r, world, eps, kind="dot")
+        total += mod.partial(hidden)
+    out = mod.finish(total, hidden)
+    ref = O.post_attn_mlp(_np(hidden), _np(mlp_w), _np(wgu), _np(wd), eps, "bfloat16")
+    torch.testing.assert_close(out.float().cpu(), torch.from_numpy(ref), **TOL)
