@@ -84,6 +84,23 @@ SIGNATURES: dict[str, tuple] = {
             c_vp,                        # stream
         ],
     ),
+    "fd_tp_exchange_bytes": (c_size, [c_i32, c_i32, c_i64]),
+    "fd_tp_exchange_alloc": (c_i32, [c_i32, c_i32, c_i64, ctypes.POINTER(c_vp)]),
+    "fd_tp_exchange_free": (c_i32, [c_vp]),
+    "fd_tp_exchange_handle": (c_i32, [c_vp, c_vp]),
+    "fd_tp_exchange_open": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
+    "fd_tp_exchange_close": (c_i32, [c_vp]),
+    "fd_post_attn_mlp_tp_out": (
+        c_i32,
+        [
+            c_vp, c_vp, c_i32,           # hidden, norm_w, norm_dtype
+            c_vp, c_i64, c_vp, c_i64,    # w_gate_up, s_gu, w_down, s_down
+            c_vp, c_i32, c_i32, c_i64, c_i64,  # out, dtype, m, h, i
+            c_f32, c_i32, c_i32, c_i32,  # eps, kind, rank, world
+            c_vp, c_i32,                 # exchange (void* const*), m_max
+            c_vp, c_size, c_vp,          # workspace, bytes, stream
+        ],
+    ),
     "fd_post_attn_mlp_workspace_bytes": (c_size, [c_i32, c_i64, c_i64]),
     "fd_post_attn_mlp_out": (
         c_i32,

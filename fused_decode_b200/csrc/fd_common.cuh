@@ -172,6 +172,32 @@ FD_DEV float warp_sum(float v) {
 
 }  // namespace fd
 
+// ------------------------------------------------- tensor-parallel exchange
+// One rank's exchange buffer (device memory every rank of the group maps):
+//   [header: sequence word, done counter; 256 B]
+//   [flags: 2 parities x world x nblk int32, 256-byte padded]
+//   [data:  2 parities x world x m_max x n fp32]
+// Round s uses parity s & 1: rank r stores block b's partial of column c at
+// data[s & 1][r][c][b*128 ...] in every rank's buffer and then sets
+// flags[s & 1][r][b] = s + 1 there.  Two parities let a rank run one round
+// ahead of a slower peer without overwriting what the peer still reads.
+constexpr int kMaxTpWorld = 8;
+constexpr int kTpBlockRows = 128;
+
+struct TpLayout {
+  int64_t nblk, flags_off, data_off, bytes;
+};
+
+__host__ __device__ inline TpLayout tp_layout(int world, int m_max, int64_t n) {
+  TpLayout l;
+  l.nblk = (n + kTpBlockRows - 1) / kTpBlockRows;
+  l.flags_off = 256;
+  const int64_t flags_bytes = ((2 * world * l.nblk * 4 + 255) / 256) * 256;
+  l.data_off = l.flags_off + flags_bytes;
+  l.bytes = l.data_off + 2LL * world * m_max * n * 4;
+  return l;
+}
+
 // Host-side helpers shared by the entry points.
 namespace fd_host {
 
@@ -201,6 +227,11 @@ inline bool same_grid(const fd_rows* l, const fd_rows* r) {
 }
 
 int sm_count();
+
+// Finish a tensor-parallel MLP layer (fd_tp.cu): out = round(sum of the
+// ranks' partials in `buf` + res), after the round's flags.
+int tp_reduce_launch(char* buf, int world, int m, int m_max, int64_t n, const void* res, void* out, int dtype,
+                     int* status, cudaStream_t st);
 
 // Launch `kernel` on `stream` as a programmatic dependent of the previous
 // kernel in the stream (see grid_dep_wait).

@@ -365,6 +365,40 @@ int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dt
                    add_residual != 0, dtype, m, h, i, eps, kind, carve(workspace), static_cast<cudaStream_t>(stream));
 }
 
+int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
+                            int64_t s_gu, const void* w_down, int64_t s_down, void* out, int32_t dtype, int32_t m,
+                            int64_t h, int64_t i, float eps, int32_t kind, int32_t rank, int32_t world,
+                            void* const* exchange, int32_t m_max, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  using namespace fd_host;
+  int r = check_mlp_args(hidden, norm_w, norm_dtype, w_gate_up, s_gu, dtype, m, h, i, kind);
+  if (r != FD_OK) return r;
+  if (world < 1 || world > kMaxTpWorld || rank < 0 || rank >= world || !exchange) return FD_ERR_ARG;
+  if (m_max < 1 || m_max > MT_MAX || m > m_max) return FD_ERR_ARG;
+  for (int k = 0; k < world; ++k)
+    if (!exchange[k]) return FD_ERR_ARG;
+  if (m == 0 || h == 0) return FD_OK;
+  r = check_down(w_down, s_down, out, dtype, dtype, i);
+  if (r != FD_OK) return r;
+  if (!workspace || workspace_bytes < fd_post_attn_mlp_workspace_bytes(m, h, i)) return FD_ERR_WORKSPACE;
+  const Workspace ws = carve(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* mid = ws.tail;
+  r = launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, dtype, m, h, i, eps, kind, ws, st);
+  if (r != FD_OK) return r;
+  // down projection of this rank's shard: block partials go to every rank
+  const TpLayout l = tp_layout(world, m_max, h);
+  GemvArgs b = {};
+  b.m = m; b.n = h; b.k = i;
+  for (int k = 0; k < world; ++k) b.tp_peer[k] = static_cast<char*>(exchange[k]);
+  b.tp_rank = rank; b.tp_world = world; b.tp_mmax = m_max;
+  b.tp_nblk = l.nblk; b.tp_flags_off = l.flags_off; b.tp_data_off = l.data_off;
+  b.tp_seq = static_cast<const int*>(exchange[rank]);
+  r = launch_linear(mid, i, w_down, s_down, b, dtype, kind, ws, st);
+  if (r != FD_OK) return r;
+  return tp_reduce_launch(static_cast<char*>(exchange[rank]), world, m, m_max, h, hidden, out, dtype, ws.status, st);
+}
+
 int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers, const void* const* norm_w, int32_t norm_dtype,
                                const void* const* w_gate_up, int64_t s_gu, const void* const* w_down,
                                int64_t s_down, void* out, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps,

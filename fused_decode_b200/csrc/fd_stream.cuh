@@ -92,6 +92,13 @@ struct GemvArgs {
   const void* norm_w;
   int32_t norm_dtype;
   float eps;
+  // tensor-parallel exchange (LINEAR mode, tp_world > 0): each finished
+  // block's fp32 partial goes to every rank's exchange buffer, followed by a
+  // flag, instead of to y (layout: TpLayout in fd_common.cuh)
+  char* tp_peer[kMaxTpWorld];
+  int32_t tp_rank, tp_world, tp_mmax;
+  int64_t tp_nblk, tp_flags_off, tp_data_off;
+  const int* tp_seq;  // this rank's sequence word (the exchange round's number)
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -227,6 +234,42 @@ struct Acc {
 };
 
 // ------------------------------------------------------------ epilogues
+FD_DEV void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Tensor-parallel publication of block blk's fp32 partial (rows of this
+// rank's down-projection shard, no residual): stored into every rank's
+// exchange buffer -- peers' buffers through NVLink peer mappings -- then, once
+// every consumer thread's stores are fenced at system scope, one flag per
+// rank is released with the round's number.  All consumer threads.
+template <int NT>
+FD_DEV void tp_publish(const GemvArgs& a, int64_t blk, const Acc<NT>& acc) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int seq = *reinterpret_cast<const volatile int*>(a.tp_seq);
+  const int par = seq & 1;
+  for (int rk = 0; rk < a.tp_world; ++rk) {
+    float* d = reinterpret_cast<float*>(a.tp_peer[rk] + a.tp_data_off) +
+               static_cast<int64_t>(par * a.tp_world + a.tp_rank) * a.tp_mmax * a.n;
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
+        const int col = 8 * t + 2 * q + (e & 1);
+        if (row < a.n && col < a.m) d[col * a.n + row] = acc.v[t][e];
+      }
+  }
+  __threadfence_system();
+  consumer_sync();
+  if (threadIdx.x < a.tp_world) {
+    int* f = reinterpret_cast<int*>(a.tp_peer[threadIdx.x] + a.tp_flags_off) +
+             static_cast<int64_t>(par * a.tp_world + a.tp_rank) * a.tp_nblk + blk;
+    st_release_sys(f, seq + 1);
+  }
+}
+
 template <typename T, int NT, int MODE>
 struct Epilogue;
 
@@ -257,6 +300,10 @@ struct Epilogue<T, NT, MODE_LINEAR> {
   FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& ex, float* /*xchg*/) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
+    if (a.tp_world > 0) {
+      tp_publish(a, blk, acc);
+      return;
+    }
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
 #pragma unroll

@@ -364,6 +364,39 @@ def post_attn_mlp_stack_out(
     _capi.check(status, "fd_post_attn_mlp_stack_out")
 
 
+def post_attn_mlp_tp_out(
+    hidden2: torch.Tensor,
+    norm_weight: torch.Tensor,
+    w_gate_up_shard: torch.Tensor,
+    w_down_shard: torch.Tensor,
+    out2: torch.Tensor,
+    eps: float,
+    kind: str,
+    exchange,
+) -> None:
+    """One tensor-parallel MLP layer whose allreduce runs over the NVLink
+    exchange buffers of ``exchange`` (a ``fused_decode_b200.tp.TPExchange``):
+    ``out2 = round(sum over ranks of the shard partials + hidden2)``."""
+    m, h = hidden2.shape
+    i = w_down_shard.shape[1]
+    if m > exchange.m_max:
+        raise ValueError(f"batch {m} exceeds the exchange's m_max={exchange.m_max}")
+    if h != exchange.hidden:
+        raise ValueError(f"hidden width {h} does not match the exchange's {exchange.hidden}")
+    lib = _capi.load()
+    ws = WORKSPACES.get(hidden2.device, lib.fd_post_attn_mlp_workspace_bytes(m, h, i))
+    status = lib.fd_post_attn_mlp_tp_out(
+        hidden2.data_ptr(), norm_weight.data_ptr(), _capi.dtype_code(norm_weight.dtype),
+        w_gate_up_shard.data_ptr(), int(w_gate_up_shard.stride(0)),
+        w_down_shard.data_ptr(), int(w_down_shard.stride(0)),
+        out2.data_ptr(), _capi.dtype_code(hidden2.dtype), m, h, i, float(eps),
+        _capi.FD_KIND_DOT if kind == "dot" else _capi.FD_KIND_SIMT,
+        exchange.rank, exchange.world, exchange.pointers, exchange.m_max,
+        ws.data_ptr(), ws.numel(), _capi.stream_of(hidden2),
+    )
+    _capi.check(status, "fd_post_attn_mlp_tp_out")
+
+
 def mlp_gate_up_out(
     hidden2: torch.Tensor,
     norm_weight: torch.Tensor,

@@ -97,7 +97,8 @@ size_t fd_linear_workspace_bytes(int32_t m, int64_t n, int64_t k);
 
 /* Byte offset, inside any workspace above, of a 32-bit status word the
  * kernels OR error bits into (1: a consumer's shared-memory pipeline wait
- * expired, 2: a producer's wait expired).  Zero means no error.  After a non-zero
+ * expired, 2: a producer's wait expired, 8: a tensor-parallel exchange wait
+ * expired).  Zero means no error.  After a non-zero
  * status the outputs of that launch are invalid and the workspace must be
  * zero-filled again before reuse. */
 size_t fd_workspace_status_offset(void);
@@ -178,6 +179,43 @@ int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers,
                                void* out, int32_t dtype, int32_t m, int64_t h, int64_t i,
                                float eps, int32_t kind, void* workspace,
                                size_t workspace_bytes, void* stream);
+
+/* ---- tensor-parallel MLP over NVLink (no counterpart in the reference,
+ * which has no multi-GPU code; this is its post_attn_mlp, ops.py:283-315,
+ * split Megatron-style across `world` GPUs of one node).
+ *
+ * Every rank owns one exchange buffer of fd_tp_exchange_bytes(world, m_max, n)
+ * bytes (n = hidden width, m_max = the largest batch it will carry, <= 16)
+ * and maps every other rank's through CUDA IPC: fd_tp_exchange_alloc (zeroed
+ * device memory), fd_tp_exchange_handle (64-byte IPC handle to share with the
+ * other ranks), fd_tp_exchange_open / _close (map / unmap a peer's buffer),
+ * fd_tp_exchange_free.  The buffers carry a round number, so a group must
+ * call fd_post_attn_mlp_tp_out the same number of times on every rank, in
+ * the same order. */
+size_t fd_tp_exchange_bytes(int32_t world, int32_t m_max, int64_t n);
+int fd_tp_exchange_alloc(int32_t world, int32_t m_max, int64_t n, void** buf);
+int fd_tp_exchange_free(void* buf);
+int fd_tp_exchange_handle(void* buf, void* handle);
+int fd_tp_exchange_open(const void* handle, void** peer);
+int fd_tp_exchange_close(void* peer);
+
+/* One tensor-parallel post_attn_mlp layer on rank `rank` of `world`:
+ * w_gate_up is this rank's [2*i, h] restack (its gate rows over the matching
+ * up rows), w_down its [h, i] column slice; hidden [m, h] is replicated.
+ * Launches the gate/up kernel, the down-projection kernel -- whose block
+ * partials go straight into every rank's exchange buffer (`exchange` holds
+ * world device pointers: this rank's buffer at [rank], the mapped peer
+ * buffers elsewhere) -- and a kernel that waits (bounded) for all ranks'
+ * partials, sums them in rank order and writes out = round(sum + hidden),
+ * the same bits on every rank.  A wait that expires sets bit 8 of the
+ * workspace status word.  Workspace: fd_post_attn_mlp_workspace_bytes(m, h, i). */
+int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm_dtype,
+                            const void* w_gate_up, int64_t s_gu,
+                            const void* w_down, int64_t s_down,
+                            void* out, int32_t dtype, int32_t m, int64_t h, int64_t i,
+                            float eps, int32_t kind, int32_t rank, int32_t world,
+                            void* const* exchange, int32_t m_max,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* First kernel of fd_post_attn_mlp_out on its own: mid[m, i] (contiguous) =
  * round(silu(gate) * up) of the RMSNorm'd hidden rows.  Replaces the

@@ -176,3 +176,99 @@ def test_tp_decode_block_llama70b(m):
     out = mod.finish(total, hidden)
     ref = O.post_attn_mlp(_np(hidden), _np(mlp_w), _np(wgu), _np(wd), eps, "bfloat16")
     torch.testing.assert_close(out.float().cpu(), torch.from_numpy(ref), **TOL)
+
+
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_tp_exchange_single_rank(m):
+    """The NVLink-exchange layer (down-projection partials published into the
+    exchange buffer, then the reduce kernel) with a group of one: equal bit
+    for bit to post_attn_mlp, round after round (the buffer's two parities
+    alternate), inside a CUDA graph too, and the status word stays clear."""
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200 import post_attn_mlp
+    from fused_decode_b200.stack import MlpStack
+
+    h, i = 1024, 2816
+    ex = tp.TPExchange(h, m_max=16)
+    try:
+        layers = [_layer(h, i, m, 900 + l)[1:] for l in range(3)]
+        x0 = _layer(h, i, m, 950)[0]
+        x = x0
+        for rnd in range(5):  # several rounds on the same buffer
+            nw, wgu, wd = layers[rnd % 3]
+            mod = tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)
+            got = mod(x)
+            want = post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot")
+            assert torch.equal(got, want), rnd
+            x = got
+        ref = _np(x0)
+        for rnd in range(5):
+            nw, wgu, wd = layers[rnd % 3]
+            ref = O.post_attn_mlp(ref, _np(nw), _np(wgu), _np(wd), EPS, "bfloat16")
+        # five chained layers: a one-ulp difference can grow, so twice the per-layer tolerance
+        torch.testing.assert_close(x.float().cpu(), torch.from_numpy(ref), rtol=2e-2, atol=2e-2)
+
+        def fn(t, nw, wgu, wd):
+            return tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)(t)
+
+        stack = MlpStack(layers, m, EPS, kind="dot", layer_fn=fn)
+        a = stack(x0).clone()
+        b = stack(x0).clone()
+        assert torch.equal(a, b)
+        y = x0
+        for nw, wgu, wd in layers:
+            y = post_attn_mlp(y, nw, wgu, wd, EPS, kind="dot")
+        assert torch.equal(a, y)
+        torch.cuda.synchronize()
+        assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+    finally:
+        ex.close()
+
+
+def _rank_main_nvlink(rank, world, port, outdir, h, i, m, layers):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ex = None
+    try:
+        dev = torch.device("cuda", rank)
+        ex = tp.TPExchange(h, m_max=16)
+        x = None
+        for layer in range(layers):
+            x0, nw, wgu, wd = _layer(h, i, m, 500 + layer, device=dev)
+            x = x0 if x is None else x
+            x = tp.TPPostAttnMlp.from_full(nw, wgu, wd, rank, world, EPS, kind="dot", exchange=ex)(x)
+        torch.cuda.synchronize()
+        np.save(os.path.join(outdir, f"rank{rank}.npy"), _np(x))
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_tp_nvlink_layers():
+    """Chained tensor-parallel layers with the NVLink exchange on 2..8 GPUs:
+    every rank ends with the same bits, equal to the unsharded oracle chain."""
+    import torch.multiprocessing as mp
+
+    h, i, m, layers = 1024, 2816, 4, 3
+    world = min(torch.cuda.device_count(), 8)
+    while (i % world or (i // world) % 8) and world > 2:
+        world -= 1
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rank_main_nvlink, args=(world, _free_port(), d, h, i, m, layers), nprocs=world,
+                           join=True, start_method="spawn")
+        outs = [np.load(os.path.join(d, f"rank{r}.npy")) for r in range(world)]
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
+    x = None
+    for layer in range(layers):
+        x0, nw, wgu, wd = [_np(t) for t in _layer(h, i, m, 500 + layer, device="cpu")]
+        x = x0 if x is None else x
+        x = O.post_attn_mlp(x, nw, wgu, wd, EPS, "bfloat16")
+    torch.testing.assert_close(torch.from_numpy(outs[0]), torch.from_numpy(x), **TOL)
