@@ -7,8 +7,9 @@ One step = one decode step's MLP half: 32 stacked post_attn_mlp layers
 as one CUDA graph.  The metric is microseconds per layer at M=1 (M=8 is
 reported beside it) and the HBM bandwidth that implies, against the measured
 copy roof.  With N>1 GPUs (torchrun) the same 32-layer stack runs tensor-
-parallel: gate/up column-sharded, down row-sharded, one NCCL allreduce per
-layer (strong scaling: the total work is fixed).
+parallel: gate/up column-sharded, down row-sharded, one partial-sum exchange
+per layer -- over the NVLink exchange buffers by default, NCCL all_reduce with
+--tp-collective nccl (strong scaling: the total work is fixed).
 
 Rank 0 prints ONE JSON line.  --impl reference times the reference's CPU
 formulation of the same layer (the oracle port of reference.py, numpy fp32) on
@@ -398,8 +399,12 @@ def run_ours(args) -> None:
     pk = peaks()
     layers = make_layers(torch, device, LAYERS, world, rank)
 
+    exchange = None
+    if world > 1 and args.tp_collective == "nvlink":
+        exchange = tp.TPExchange(H, m_max=16)
+
     def layer_fn_tp(x, nw, wgu, wd):
-        return tp.TPPostAttnMlp(nw, wgu, wd, EPS)(x)
+        return tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=exchange)(x)
 
     def build_stack(m):
         fn = layer_fn_tp if world > 1 else None
@@ -579,7 +584,8 @@ def run_ours(args) -> None:
             "data": "synthetic (seeded random-init Llama-3-8B MLP weights, N(0,0.02))",
             "config": {
                 "workload": f"post_attn_mlp Llama-3-8B widths, M={args.m}, {LAYERS} layers in one CUDA graph"
-                            + (f", tensor-parallel x{world} (NCCL allreduce per layer)" if world > 1 else ""),
+                            + (f", tensor-parallel x{world} ({args.tp_collective} partial-sum exchange per layer)"
+                               if world > 1 else ""),
                 "hidden": H, "intermediate": I, "m": args.m, "layers": LAYERS, "kind": "dot",
                 "parallelism": f"tp{world}" if world > 1 else "single",
                 "l2": f"inputs larger than L2: {LAYERS * layer_bytes(args.m, world=world) / 1e9:.1f} GB of weights per step per GPU",
@@ -614,14 +620,17 @@ def run_ours(args) -> None:
                     "api": "fused_decode_b200.stack.MlpStack (pinned host in, graph replay, pinned host out)",
                     "eager_api_us_per_layer": e2e_eager_s * 1e6 / LAYERS},
             # single GPU: two launches per layer; tensor-parallel: gate/up, down
-            # (fp32 partial) and residual-add launches per layer (+ NCCL)
+            # and reduce (NVLink exchange) or residual-add (after NCCL) per layer
             "gpu_launches": args.steps * (stack1.launches_per_replay if world == 1 else 3 * LAYERS),
+            "tp_collective": args.tp_collective if world > 1 else None,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         del stack1, stack8, graph_gu, graph_dn
         torch.cuda.synchronize()
+        if exchange is not None:
+            exchange.close()
         dist.destroy_process_group()
 
 
@@ -698,6 +707,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="skip the standalone-op measurements")
+    ap.add_argument("--tp-collective", choices=("nvlink", "nccl"), default="nvlink",
+                    help="N>1: partial sums over the NVLink exchange buffers (default) or NCCL all_reduce")
     ap.add_argument("--ncu-case", choices=NCU_CASES, default=None,
                     help="run a small fixed workload of one kernel for an ncu capture and exit")
     args = ap.parse_args()

@@ -174,27 +174,27 @@ FD_DEV float warp_sum(float v) {
 
 // ------------------------------------------------- tensor-parallel exchange
 // One rank's exchange buffer (device memory every rank of the group maps):
-//   [header: sequence word, done counter; 256 B]
-//   [flags: 2 parities x world x nblk int32, 256-byte padded]
-//   [data:  2 parities x world x m_max x n fp32]
-// Round s uses parity s & 1: rank r stores block b's partial of column c at
-// data[s & 1][r][c][b*128 ...] in every rank's buffer and then sets
-// flags[s & 1][r][b] = s + 1 there.  Two parities let a rank run one round
-// ahead of a slower peer without overwriting what the peer still reads.
+//   [header: round number, done counter; 256 B]
+//   [data: 2 parities x world x m_max x n tagged words of 8 bytes]
+// In round s rank r stores element (c, row) of its fp32 partial as the 8-byte
+// word {value bits, s + 1} at data[s & 1][r][c][row] of every rank's buffer.
+// An aligned 8-byte store arrives whole, so a reader that sees tag s + 1 also
+// sees the value: no fence and no separate flag between writer and reader.
+// Two parities let a rank run one round ahead of a slower peer without
+// overwriting words the peer has not read yet (and a word left from round
+// s - 2 carries tag s - 1).
 constexpr int kMaxTpWorld = 8;
 constexpr int kTpBlockRows = 128;
 
 struct TpLayout {
-  int64_t nblk, flags_off, data_off, bytes;
+  int64_t nblk, data_off, bytes;
 };
 
 __host__ __device__ inline TpLayout tp_layout(int world, int m_max, int64_t n) {
   TpLayout l;
   l.nblk = (n + kTpBlockRows - 1) / kTpBlockRows;
-  l.flags_off = 256;
-  const int64_t flags_bytes = ((2 * world * l.nblk * 4 + 255) / 256) * 256;
-  l.data_off = l.flags_off + flags_bytes;
-  l.bytes = l.data_off + 2LL * world * m_max * n * 4;
+  l.data_off = 256;
+  l.bytes = l.data_off + 2LL * world * m_max * n * 8;
   return l;
 }
 

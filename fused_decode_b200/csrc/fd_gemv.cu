@@ -392,7 +392,7 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
   b.m = m; b.n = h; b.k = i;
   for (int k = 0; k < world; ++k) b.tp_peer[k] = static_cast<char*>(exchange[k]);
   b.tp_rank = rank; b.tp_world = world; b.tp_mmax = m_max;
-  b.tp_nblk = l.nblk; b.tp_flags_off = l.flags_off; b.tp_data_off = l.data_off;
+  b.tp_data_off = l.data_off;
   b.tp_seq = static_cast<const int*>(exchange[rank]);
   r = launch_linear(mid, i, w_down, s_down, b, dtype, kind, ws, st);
   if (r != FD_OK) return r;

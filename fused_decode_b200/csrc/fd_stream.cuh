@@ -97,8 +97,8 @@ struct GemvArgs {
   // flag, instead of to y (layout: TpLayout in fd_common.cuh)
   char* tp_peer[kMaxTpWorld];
   int32_t tp_rank, tp_world, tp_mmax;
-  int64_t tp_nblk, tp_flags_off, tp_data_off;
-  const int* tp_seq;  // this rank's sequence word (the exchange round's number)
+  int64_t tp_data_off;
+  const int* tp_seq;  // this rank's round number
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -234,39 +234,31 @@ struct Acc {
 };
 
 // ------------------------------------------------------------ epilogues
-FD_DEV void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+FD_DEV void st_tagged_sys(void* p, float v, int tag) {
+  asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
+               : "memory");
 }
 
 // Tensor-parallel publication of block blk's fp32 partial (rows of this
-// rank's down-projection shard, no residual): stored into every rank's
-// exchange buffer -- peers' buffers through NVLink peer mappings -- then, once
-// every consumer thread's stores are fenced at system scope, one flag per
-// rank is released with the round's number.  All consumer threads.
+// rank's down-projection shard, no residual): every element goes to every
+// rank's exchange buffer -- peers' through NVLink peer mappings -- as a word
+// tagged with the round number (layout: TpLayout).  No fence, no flag.
 template <int NT>
 FD_DEV void tp_publish(const GemvArgs& a, int64_t blk, const Acc<NT>& acc) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int seq = *reinterpret_cast<const volatile int*>(a.tp_seq);
-  const int par = seq & 1;
+  const int64_t slab = static_cast<int64_t>((seq & 1) * a.tp_world + a.tp_rank) * a.tp_mmax * a.n;
   for (int rk = 0; rk < a.tp_world; ++rk) {
-    float* d = reinterpret_cast<float*>(a.tp_peer[rk] + a.tp_data_off) +
-               static_cast<int64_t>(par * a.tp_world + a.tp_rank) * a.tp_mmax * a.n;
+    uint2* d = reinterpret_cast<uint2*>(a.tp_peer[rk] + a.tp_data_off) + slab;
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
         const int col = 8 * t + 2 * q + (e & 1);
-        if (row < a.n && col < a.m) d[col * a.n + row] = acc.v[t][e];
+        if (row < a.n && col < a.m) st_tagged_sys(d + col * a.n + row, acc.v[t][e], seq + 1);
       }
-  }
-  __threadfence_system();
-  consumer_sync();
-  if (threadIdx.x < a.tp_world) {
-    int* f = reinterpret_cast<int*>(a.tp_peer[threadIdx.x] + a.tp_flags_off) +
-             static_cast<int64_t>(par * a.tp_world + a.tp_rank) * a.tp_nblk + blk;
-    st_release_sys(f, seq + 1);
   }
 }
 

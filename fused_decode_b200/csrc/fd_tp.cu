@@ -2,11 +2,11 @@
 // (CUDA IPC), and the kernel that finishes a tensor-parallel MLP layer.
 //
 // The down-projection kernel of every rank stores its fp32 block partials
-// straight into every rank's exchange buffer and releases one flag per block
-// (tp_publish, fd_stream.cuh).  tp_reduce_kernel then waits -- bounded -- for
-// the flags of its blocks from all ranks, sums the partials in rank order (the
-// same order on every rank, so all ranks produce identical bits), adds the
-// residual and rounds: out = round(sum_r partial_r + hidden).  This replaces
+// straight into every rank's exchange buffer as words tagged with the round
+// number (tp_publish, fd_stream.cuh).  tp_reduce_kernel then waits -- bounded
+// -- for each word's tag, sums the partials in rank order (the same order on
+// every rank, so all ranks produce identical bits), adds the residual and
+// rounds: out = round(sum_r partial_r + hidden).  This replaces
 // an NCCL allreduce plus a residual-add launch; no kernel issues a TMA load
 // from peer memory, and nothing uses NVLink multicast.
 #include "fd_common.cuh"
@@ -27,59 +27,60 @@ FD_DEV uint64_t gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-FD_DEV int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 struct TpReduceArgs {
   char* buf;  // this rank's exchange buffer
   int32_t world, m, m_max;
-  int64_t n, nblk, flags_off, data_off;
+  int64_t n, data_off;
   const void* res;  // residual [m, n] (contiguous)
   void* out;        // [m, n] (contiguous)
   int* status;
 };
 
-// One CTA per 128-row block.  Launched as a programmatic dependent of the
-// down-projection kernel: it starts polling while that kernel drains, and
-// waits for it (griddepcontrol.wait) only before finishing, so the next
-// kernel, which waits for this one, also runs after the down projection.
+FD_DEV uint2 ld_tagged_sys(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+// One thread per row of a 128-row block.  Launched as a programmatic
+// dependent of the down-projection kernel: it starts reading while that
+// kernel drains, and waits for it (griddepcontrol.wait) only before
+// finishing, so the next kernel, which waits for this one, also runs after
+// the down projection.
 template <typename T>
 __global__ void __launch_bounds__(kTpBlockRows) tp_reduce_kernel(TpReduceArgs a) {
-  __shared__ int s_fail;
+  // the next layer's gate/up kernel may be scheduled now: it prefetches its
+  // weights and waits for this grid before reading anything it writes
+  grid_dep_launch();
   int* seqp = reinterpret_cast<int*>(a.buf);
   int* donep = seqp + 1;
   const int seq = *reinterpret_cast<volatile int*>(seqp);
-  const int par = seq & 1;
-  const int64_t blk = blockIdx.x;
-  if (threadIdx.x == 0) s_fail = 0;
-  __syncthreads();
-  if (threadIdx.x < a.world) {
-    const int* f = reinterpret_cast<const int*>(a.buf + a.flags_off) +
-                   static_cast<int64_t>(par * a.world + threadIdx.x) * a.nblk + blk;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kTpBlockRows + threadIdx.x;
+  if (row < a.n) {
+    const uint2* d = reinterpret_cast<const uint2*>(a.buf + a.data_off) +
+                     static_cast<int64_t>((seq & 1) * a.world) * a.m_max * a.n;
     const uint64_t t0 = gtimer();
-    while (ld_acquire_sys(f) != seq + 1) {
-      if (gtimer() - t0 > kTpWaitNs) {
-        atomicOr(a.status, kStatusTpTimeout);
-        s_fail = 1;
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  __syncthreads();
-  const int64_t row = blk * kTpBlockRows + threadIdx.x;
-  if (!s_fail && row < a.n) {
-    const float* d = reinterpret_cast<const float*>(a.buf + a.data_off) +
-                     static_cast<int64_t>(par * a.world) * a.m_max * a.n;
-    for (int col = 0; col < a.m; ++col) {
+    bool ok = true;
+    for (int col = 0; col < a.m && ok; ++col) {
       float sum = 0.f;
-      for (int rk = 0; rk < a.world; ++rk) sum += __ldcg(d + (static_cast<int64_t>(rk) * a.m_max + col) * a.n + row);
+      for (int rk = 0; rk < a.world; ++rk) {  // rank order: the same sum on every rank
+        const uint2* w = d + (static_cast<int64_t>(rk) * a.m_max + col) * a.n + row;
+        uint2 v = ld_tagged_sys(w);
+        while (static_cast<int>(v.y) != seq + 1) {
+          if (gtimer() - t0 > kTpWaitNs) {
+            atomicOr(a.status, kStatusTpTimeout);
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+          v = ld_tagged_sys(w);
+        }
+        sum += __uint_as_float(v.x);
+      }
       const int64_t o = col * a.n + row;
       sum += to_f32(static_cast<const T*>(a.res)[o]);
-      static_cast<T*>(a.out)[o] = from_f32<T>(sum);
+      if (ok) static_cast<T*>(a.out)[o] = from_f32<T>(sum);
     }
   }
   // The last CTA to finish advances this rank's round number.
@@ -106,7 +107,7 @@ int tp_reduce_launch(char* buf, int world, int m, int m_max, int64_t n, const vo
   TpReduceArgs a;
   a.buf = buf;
   a.world = world; a.m = m; a.m_max = m_max;
-  a.n = n; a.nblk = l.nblk; a.flags_off = l.flags_off; a.data_off = l.data_off;
+  a.n = n; a.data_off = l.data_off;
   a.res = res; a.out = out; a.status = status;
   const dim3 grid(static_cast<unsigned>(l.nblk));
   const cudaError_t e = dtype == FD_BF16 ? launch_pdl(tp_reduce_kernel<__nv_bfloat16>, grid, kTpBlockRows, 0, st, a)
