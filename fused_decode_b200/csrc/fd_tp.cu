@@ -43,11 +43,12 @@ FD_DEV uint2 ld_tagged_sys(const uint2* p) {
   return v;
 }
 
-// One thread per row of a 128-row block.  Launched as a programmatic
-// dependent of the down-projection kernel: it starts reading while that
-// kernel drains, and waits for it (griddepcontrol.wait) only before
-// finishing, so the next kernel, which waits for this one, also runs after
-// the down projection.
+// One thread per (row, column): grid (row blocks of 128, m).  The words of
+// all ranks are loaded together (one round trip), then any whose tag is not
+// yet this round's is re-read, bounded.  Launched as a programmatic dependent
+// of the down-projection kernel: it starts reading while that kernel drains,
+// and waits for it (griddepcontrol.wait) only before finishing, so the next
+// kernel, which waits for this one, also runs after the down projection.
 template <typename T>
 __global__ void __launch_bounds__(kTpBlockRows) tp_reduce_kernel(TpReduceArgs a) {
   // the next layer's gate/up kernel may be scheduled now: it prefetches its
@@ -57,37 +58,46 @@ __global__ void __launch_bounds__(kTpBlockRows) tp_reduce_kernel(TpReduceArgs a)
   int* donep = seqp + 1;
   const int seq = *reinterpret_cast<volatile int*>(seqp);
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kTpBlockRows + threadIdx.x;
+  const int col = blockIdx.y;
   if (row < a.n) {
     const uint2* d = reinterpret_cast<const uint2*>(a.buf + a.data_off) +
-                     static_cast<int64_t>((seq & 1) * a.world) * a.m_max * a.n;
-    const uint64_t t0 = gtimer();
+                     (static_cast<int64_t>((seq & 1) * a.world) * a.m_max + col) * a.n + row;
+    const int64_t rank_stride = static_cast<int64_t>(a.m_max) * a.n;
+    uint2 v[kMaxTpWorld];
+#pragma unroll
+    for (int rk = 0; rk < kMaxTpWorld; ++rk)
+      if (rk < a.world) v[rk] = ld_tagged_sys(d + rk * rank_stride);
     bool ok = true;
-    for (int col = 0; col < a.m && ok; ++col) {
-      float sum = 0.f;
-      for (int rk = 0; rk < a.world; ++rk) {  // rank order: the same sum on every rank
-        const uint2* w = d + (static_cast<int64_t>(rk) * a.m_max + col) * a.n + row;
-        uint2 v = ld_tagged_sys(w);
-        while (static_cast<int>(v.y) != seq + 1) {
+    const uint64_t t0 = gtimer();
+#pragma unroll
+    for (int rk = 0; rk < kMaxTpWorld; ++rk) {
+      if (rk < a.world && ok) {
+        while (static_cast<int>(v[rk].y) != seq + 1) {
           if (gtimer() - t0 > kTpWaitNs) {
             atomicOr(a.status, kStatusTpTimeout);
             ok = false;
             break;
           }
           __nanosleep(32);
-          v = ld_tagged_sys(w);
+          v[rk] = ld_tagged_sys(d + rk * rank_stride);
         }
-        sum += __uint_as_float(v.x);
       }
+    }
+    if (ok) {
+      float sum = 0.f;
+#pragma unroll
+      for (int rk = 0; rk < kMaxTpWorld; ++rk)  // rank order: the same sum on every rank
+        if (rk < a.world) sum += __uint_as_float(v[rk].x);
       const int64_t o = col * a.n + row;
       sum += to_f32(static_cast<const T*>(a.res)[o]);
-      if (ok) static_cast<T*>(a.out)[o] = from_f32<T>(sum);
+      static_cast<T*>(a.out)[o] = from_f32<T>(sum);
     }
   }
   // The last CTA to finish advances this rank's round number.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    if (atomicAdd(donep, 1) == static_cast<int>(gridDim.x) - 1) {
+    if (atomicAdd(donep, 1) == static_cast<int>(gridDim.x * gridDim.y) - 1) {
       *donep = 0;
       *reinterpret_cast<volatile int*>(seqp) = seq + 1;
     }
@@ -109,7 +119,7 @@ int tp_reduce_launch(char* buf, int world, int m, int m_max, int64_t n, const vo
   a.world = world; a.m = m; a.m_max = m_max;
   a.n = n; a.data_off = l.data_off;
   a.res = res; a.out = out; a.status = status;
-  const dim3 grid(static_cast<unsigned>(l.nblk));
+  const dim3 grid(static_cast<unsigned>(l.nblk), static_cast<unsigned>(m));
   const cudaError_t e = dtype == FD_BF16 ? launch_pdl(tp_reduce_kernel<__nv_bfloat16>, grid, kTpBlockRows, 0, st, a)
                                          : launch_pdl(tp_reduce_kernel<__half>, grid, kTpBlockRows, 0, st, a);
   return from_cuda(e);
