@@ -182,6 +182,17 @@ def cpu_time_layers(x, layers, budget_s: float, min_evals: int, max_evals: int |
     return statistics.median(times) * 1e6, len(times), threads
 
 
+def workload_config(m: int, world: int, collective: str) -> dict:
+    """The `config` object both arms print: the workload the metric is quoted on."""
+    return {
+        "workload": f"post_attn_mlp Llama-3-8B widths, M={m}, {LAYERS} layers in one CUDA graph"
+                    + (f", tensor-parallel x{world} ({collective} partial-sum exchange per layer)" if world > 1 else ""),
+        "hidden": H, "intermediate": I, "m": m, "layers": LAYERS, "kind": "dot",
+        "parallelism": f"tp{world}" if world > 1 else "single",
+        "l2": f"inputs larger than L2: {LAYERS * layer_bytes(m, world=world) / 1e9:.1f} GB of weights per step per GPU",
+    }
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU formulation (oracle port) on host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -191,14 +202,14 @@ def run_reference(args) -> None:
     x, layers = cpu_layer_sample(2, m)
     cpu_time_layers(x, layers, 0.0, max(1, args.warmup), max(1, args.warmup))  # warm-up
     us, evals, threads = cpu_time_layers(x, layers, 0.0, args.steps, args.steps)
-    sample = f"{evals} single-layer steps over 2 seeded Llama-3-8B MLP layers, M={m}, numpy fp32 (oracle port of reference.py:66-79)"
+    sample = (f"{evals} single-layer steps over 2 seeded Llama-3-8B MLP layers, M={m}, numpy fp32 "
+              f"(oracle port of reference.py:66-79) on the host cores; each step is one layer of the workload")
     line = {
         "impl": "reference", "metric": METRIC, "value": us, "unit": "us/layer",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3,
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights rounded to bf16)",
-        "config": {"workload": f"post_attn_mlp Llama-3-8B widths M={m} (CPU, one layer per step)",
-                   "hidden": H, "intermediate": I, "m": m},
+        "config": workload_config(m, args.gpus, args.tp_collective),
         "cpu_baseline": {"value": us, "unit": "us/layer", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": us, "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -582,14 +593,7 @@ def run_ours(args) -> None:
             "vs_baseline": us1 / PUBLISHED_US[1] if args.m == 1 else None,
             "dtype": "bf16",
             "data": "synthetic (seeded random-init Llama-3-8B MLP weights, N(0,0.02))",
-            "config": {
-                "workload": f"post_attn_mlp Llama-3-8B widths, M={args.m}, {LAYERS} layers in one CUDA graph"
-                            + (f", tensor-parallel x{world} ({args.tp_collective} partial-sum exchange per layer)"
-                               if world > 1 else ""),
-                "hidden": H, "intermediate": I, "m": args.m, "layers": LAYERS, "kind": "dot",
-                "parallelism": f"tp{world}" if world > 1 else "single",
-                "l2": f"inputs larger than L2: {LAYERS * layer_bytes(args.m, world=world) / 1e9:.1f} GB of weights per step per GPU",
-            },
+            "config": workload_config(args.m, world, args.tp_collective),
             "hbm_gbs": gbs1,
             "hbm_frac": gbs1 / pk["hbm_gbs"],
             "copy_roof_gbs": roof,
