@@ -51,6 +51,9 @@ __global__ void __launch_bounds__(MAXT, MINB)
   __syncthreads();
 
   if (warp == GW + P) {
+    // The split-K counters are shared with the previous launch on this
+    // workspace: look at them only once that launch has completed.
+    grid_dep_wait();
     if (lane == 0) {
       announce_mid(a, ms, s0, s1, G, &s_abort);
       if (MODE == MODE_GATEUP) watch_final(a, ms, s0, s1, G, c);

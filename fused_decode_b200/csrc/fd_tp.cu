@@ -45,12 +45,12 @@ FD_DEV uint2 ld_tagged_sys(const uint2* p) {
 
 // One thread per (row, column): grid (row blocks of 128, m).  The words of
 // all ranks are loaded together (one round trip), then any whose tag is not
-// yet this round's is re-read, bounded.  Launched as a programmatic dependent
-// of the down-projection kernel: it starts reading while that kernel drains,
-// and waits for it (griddepcontrol.wait) only before finishing, so the next
-// kernel, which waits for this one, also runs after the down projection.
+// yet this round's is re-read, bounded.
 template <typename T>
 __global__ void __launch_bounds__(kTpBlockRows) tp_reduce_kernel(TpReduceArgs a) {
+  // The round number was advanced by the previous round's reduce, which has
+  // completed once the down-projection kernel before this one has.
+  grid_dep_wait();
   // the next layer's gate/up kernel may be scheduled now: it prefetches its
   // weights and waits for this grid before reading anything it writes
   grid_dep_launch();
@@ -102,7 +102,6 @@ __global__ void __launch_bounds__(kTpBlockRows) tp_reduce_kernel(TpReduceArgs a)
       *reinterpret_cast<volatile int*>(seqp) = seq + 1;
     }
   }
-  grid_dep_wait();
 }
 
 int from_cuda(cudaError_t e) { return e == cudaSuccess ? FD_OK : FD_ERR_LAUNCH; }

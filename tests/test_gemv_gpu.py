@@ -237,6 +237,27 @@ def test_post_attn_mlp_stack_fused(m):
         torch.testing.assert_close(stack(x0), fused_out, rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("m", [1, 5])
+def test_post_attn_mlp_stack_deterministic(m):
+    """A stack of back-to-back launches (programmatic dependent launches, one
+    shared split-K workspace) gives the same bits every time, equal to
+    separate calls: no launch may read the previous launch's split-K state."""
+    h, i, layers = 512, 1024, 6
+    dtype = torch.bfloat16
+    ws = [_mlp_weights(h, i, dtype, 300 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(31 + m))
+    x = x0
+    for nw, wgu, wd in ws:
+        x = post_attn_mlp(x, nw, wgu, wd, 1e-5)
+    outs = []
+    for _ in range(40):
+        o = torch.empty_like(x0)
+        K.post_attn_mlp_stack_out(x0, ws, o, 1e-5, "dot")
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert all(torch.equal(o, x) for o in outs)
+
+
 def test_post_attn_mlp_stack_many_layers():
     """35 layers: the ping-pong buffers alternate an odd number of times."""
     h, i, layers, m = 128, 256, 35, 3
