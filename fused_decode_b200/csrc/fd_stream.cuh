@@ -651,18 +651,37 @@ FD_DEV void load8_smem_as_f32(const unsigned char* p, int dtype, float* f) {
   }
 }
 
+// JV: 16-byte vectors per thread per row (compile-time, so the row / vector
+// split of the register batch folds away; 0 = rows too wide for one batch).
+template <typename T, int JV>
+FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
+                      uint64_t* nw_bar);
+
 template <typename T>
 FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
                          uint64_t* nw_bar) {
+  const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
+  switch ((nvec_pad + CONSUMERS - 1) / CONSUMERS) {
+    case 1: norm_rows<T, 1>(a, r, s_sumsq, nw, nw_bar); break;
+    case 2: norm_rows<T, 2>(a, r, s_sumsq, nw, nw_bar); break;
+    case 3: norm_rows<T, 3>(a, r, s_sumsq, nw, nw_bar); break;
+    case 4: norm_rows<T, 4>(a, r, s_sumsq, nw, nw_bar); break;
+    default: norm_rows<T, 0>(a, r, s_sumsq, nw, nw_bar); break;
+  }
+}
+
+template <typename T, int JV>
+FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
+                      uint64_t* nw_bar) {
   constexpr int REGS = 8;  // 16-byte vectors of hidden held per thread per group
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned char* xs = r.xreg;
   const int nvec = static_cast<int>(a.k / 8);
   const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
-  const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;  // vectors per thread per row
+  constexpr int jv = JV;
   const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
-  if (jv <= 4) {
-    const int rows_per_group = REGS / jv;
+  if constexpr (JV > 0) {
+    constexpr int rows_per_group = REGS / JV;
     for (int r0 = 0; r0 < a.m; r0 += rows_per_group) {
       const int nr = min(rows_per_group, a.m - r0);
       uint4 hv[REGS];
@@ -725,7 +744,7 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
       consumer_sync();  // s_sumsq is reused by the next group
     }
     return;
-  }
+  } else {
   // Very wide rows: two passes per row, loads of a pass in flight together.
   for (int mrow = 0; mrow < a.m; ++mrow) {
     const uint4* hr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride);
@@ -758,6 +777,7 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
       st_shared16(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4), packed);
     }
     consumer_sync();
+  }
   }
 }
 
