@@ -719,22 +719,27 @@ FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]
       }
       consumer_sync();
       if (r0 == 0 && !mbar_wait(nw_bar, 0)) atomicOr(a.status, kStatusFullTimeout);
+      // one scale per row of the group, then a short loop over the vectors
+      float inv[rows_per_group];
+#pragma unroll
+      for (int rr = 0; rr < rows_per_group; ++rr) {
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < GW; ++w) tot += s_sumsq[w][rr];
+        inv[rr] = rr < nr ? rsqrtf(tot / static_cast<float>(a.k) + a.eps) : 0.f;  // rows past m: unused
+      }
 #pragma unroll
       for (int e = 0; e < REGS; ++e) {
         const int rr = e / jv, j = e - (e / jv) * jv;
         const int v = tid + j * CONSUMERS;
         if (rr < nr && v < nvec_pad) {
-          float tot = 0.f;
-#pragma unroll
-          for (int w = 0; w < GW; ++w) tot += s_sumsq[w][rr];
-          const float inv = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
           uint4 packed = make_uint4(0, 0, 0, 0);
           if (v < nvec) {
             float f[8], w[8], o[8];
             unpack8<T>(hv[e], f);
             load8_smem_as_f32(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, w);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) o[q] = f[q] * inv * w[q];
+            for (int q = 0; q < 8; ++q) o[q] = f[q] * inv[rr] * w[q];
             packed = pack8<T>(o);
           }
           const int mrow = r0 + rr, chunk = v >> 3, cc = v & 7;
