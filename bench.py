@@ -42,7 +42,7 @@ METRIC = "post_attn_mlp us/layer at M=1 (Llama-3-8B widths, 32-layer CUDA graph)
 def layer_bytes(m: int, h: int = H, i: int = I, world: int = 1) -> int:
     """Algorithmic HBM bytes of one layer on one rank: weights once, hidden in,
     out, norm weight.  Intermediates stay in L2 and are not counted."""
-    return (2 * i * h + h * i) * 2 // world + 3 * m * h * 2 if m else 0
+    return (2 * i * h + h * i) * 2 // world + 2 * m * h * 2 + h * 2 if m else 0
 
 
 def gate_up_launch_bytes(m: int, world: int = 1) -> int:
