@@ -229,7 +229,7 @@ inline bool same_grid(const fd_rows* l, const fd_rows* r) {
 int sm_count();
 
 // Finish a tensor-parallel MLP layer (fd_tp.cu): out = round(sum of the
-// ranks' partials in `buf` + res), after the round's flags.
+// ranks' partials in `buf` + res), once every word carries the round's tag.
 int tp_reduce_launch(char* buf, int world, int m, int m_max, int64_t n, const void* res, void* out, int dtype,
                      int* status, cudaStream_t st);
 
