@@ -26,3 +26,6 @@ __all__ = [
     "swiglu",
 ]
 __version__ = "0.1.0"
+
+# torch.ops.fused_decode_b200.* (custom ops with fake implementations)
+from fused_decode_b200 import library  # noqa: E402,F401
