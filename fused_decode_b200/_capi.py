@@ -166,6 +166,38 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
+_fast = None
+
+
+def fast():
+    """The compiled dispatch module ``_fastpath`` (csrc/fd_fastpath.cpp), loaded
+    once; like ``load()`` it fails loudly when it has not been built."""
+    global _fast
+    if _fast is None:
+        load()
+        try:
+            from fused_decode_b200 import _fastpath
+        except ImportError as exc:
+            raise RuntimeError(
+                "the _fastpath extension is not built (or does not load): "
+                "build it with `python -m fused_decode_b200.build`"
+            ) from exc
+        _fast = _fastpath
+    return _fast
+
+
+def fast_or_none():
+    """``fast()``, or None when either native module is missing.  The
+    operators use this to offer a call to the compiled path first; when it is
+    absent their Python path still fails loudly at the launch (``load()``)."""
+    if _fast is not None:
+        return _fast
+    try:
+        return fast()
+    except RuntimeError:
+        return None
+
+
 def dtype_code(dtype: torch.dtype) -> int:
     try:
         return _DTYPE_CODE[dtype]

@@ -1,8 +1,9 @@
-"""Build ``libfd_b200.so`` from ``csrc/*.cu`` for sm_100a with nvcc.
+"""Build ``libfd_b200.so`` from ``csrc/*.cu`` for sm_100a with nvcc, then the
+``_fastpath`` Python extension (``csrc/fd_fastpath.cpp``) that calls it.
 
-``python -m fused_decode_b200.build`` (or ``__graft_entry__.build()``).  The
-library is written next to this file so it travels with the source tree.
-Objects are rebuilt only when a source or header is newer than the library.
+``python -m fused_decode_b200.build`` (or ``__graft_entry__.build()``).  Both
+are written next to this file so they travel with the source tree.  Each is
+rebuilt only when one of its sources or headers is newer than it.
 """
 
 from __future__ import annotations
@@ -13,6 +14,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -32,6 +34,10 @@ def _nvcc() -> str:
     return cand
 
 
+FASTPATH_SRC = os.path.join(CSRC, "fd_fastpath.cpp")
+FASTPATH_OUT = os.path.join(HERE, "_fastpath" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
 def _sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
@@ -47,7 +53,50 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(p) <= built for p in _deps())
 
 
+def _fastpath_up_to_date() -> bool:
+    if not os.path.exists(FASTPATH_OUT):
+        return False
+    built = os.path.getmtime(FASTPATH_OUT)
+    deps = [FASTPATH_SRC, OUT, *glob.glob(os.path.join(INCLUDE, "*.h"))]
+    return all(os.path.getmtime(p) <= built for p in deps)
+
+
+def build_fastpath(force: bool = False, verbose: bool = False) -> str:
+    """Compile the pybind11 / ATen extension against the installed torch and
+    link it to libfd_b200.so (found next to it at run time)."""
+    if not force and _fastpath_up_to_date():
+        return FASTPATH_OUT
+    import torch
+
+    torch_dir = os.path.dirname(torch.__file__)
+    torch_lib = os.path.join(torch_dir, "lib")
+    cuda_home = os.environ.get("CUDA_HOME") or os.path.dirname(os.path.dirname(os.path.realpath(_nvcc())))
+    incs = [os.path.join(torch_dir, "include"), os.path.join(torch_dir, "include", "torch", "csrc", "api", "include"),
+            os.path.join(cuda_home, "include"), sysconfig.get_paths()["include"]]
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}", "-I", INCLUDE]
+    for inc in incs:
+        cmd += ["-isystem", inc]
+    tmp = FASTPATH_OUT + ".tmp"
+    cmd += [FASTPATH_SRC, "-o", tmp, "-L", HERE, "-lfd_b200", "-Wl,-rpath,$ORIGIN",
+            "-L", torch_lib, f"-Wl,-rpath,{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+            "-ltorch_python"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"fastpath build failed: {' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, FASTPATH_OUT)
+    return FASTPATH_OUT
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    _build_library(force, verbose)
+    build_fastpath(force, verbose)
+    return OUT
+
+
+def _build_library(force: bool, verbose: bool) -> str:
     if not force and up_to_date():
         return OUT
     nvcc = _nvcc()

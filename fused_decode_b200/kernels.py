@@ -85,37 +85,30 @@ def _write_back(layout: RowLayout, target: torch.Tensor) -> None:
 class _WorkspaceCache:
     """One zero-initialised scratch buffer per (device, stream).
 
-    The split-K kernels leave their counters at zero when they finish, so a
-    buffer is zero-filled only when it is first allocated or grown.  Launches
-    that share a buffer must be stream-ordered, which the per-stream key
-    guarantees.
+    The buffers are held by the compiled dispatch module (``_fastpath``), so
+    the Python launchers and the compiled fast path share them.  The split-K
+    kernels leave their counters at zero when they finish, so a buffer is
+    zero-filled only when it is first allocated or grown.  Launches that share
+    a buffer must be stream-ordered, which the per-stream key guarantees.
     """
 
-    def __init__(self) -> None:
-        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
-
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        stream = torch.cuda.current_stream(device).cuda_stream
-        key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
-        buf = self._bufs.get(key)
-        if buf is None or buf.numel() < nbytes:
-            size = max(nbytes, 1 << 20)
-            buf = torch.zeros(size, dtype=torch.uint8, device=device)
-            self._bufs[key] = buf
-        return buf
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        return _capi.fast().workspace(index, int(nbytes))
 
     def clear(self) -> None:
-        self._bufs.clear()
+        _capi.fast().clear_workspaces()
 
     def status(self) -> dict:
         """Error bits of every cached workspace (synchronises the device).
 
         Non-zero means a kernel's bounded shared-memory pipeline wait expired
-        (1: consumer, 2: producer) and its output is not valid.
+        (1: consumer, 2: producer) or a tensor-parallel exchange wait expired
+        (8), and that output is not valid.
         """
         off = _capi.load().fd_workspace_status_offset()
         out = {}
-        for key, buf in self._bufs.items():
+        for key, buf in _capi.fast().workspaces():
             if buf.numel() >= off + 4:
                 out[key] = int(buf[off:off + 4].view(torch.int32).item())
         return out

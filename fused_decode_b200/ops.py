@@ -10,6 +10,12 @@ Divergence from the reference, on purpose: ``DECODE_LINEAR_MAX_M`` is 16, not
 cuBLAS won from M=2 (ops.py:16-19); the B200 kernels here cover the whole
 decode range M=1..16.  Above 16 rows (prefill) ``linear_decode`` passes through
 to ``torch.nn.functional.linear`` exactly as the reference does.
+
+Each operator first offers its arguments to the compiled dispatch module
+(``_fastpath``, csrc/fd_fastpath.cpp), which launches the common case --
+CUDA tensors of supported dtypes, at most four dimensions, no copies needed
+-- without Python in between.  It declines everything else, argument errors
+included, and the code below handles those with the same kernels.
 """
 
 from __future__ import annotations
@@ -19,6 +25,7 @@ import math
 import torch
 import torch.nn.functional as F
 
+from fused_decode_b200._capi import fast_or_none as _fast
 from fused_decode_b200.kernels import (
     GEMV_MAX_M,
     linear_out,
@@ -95,6 +102,10 @@ def rms_norm(
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """RMSNorm over the last dimension; ``weight`` is ``(N,)`` (reference ops.py:72-88)."""
+    fp = _fast()
+    done = fp.rms_norm(x, weight, eps, out) if fp is not None else None
+    if done is not None:
+        return done
     _check_activation(x, "x")
     _check_norm_weight(weight, x)
     eps = _check_eps(eps)
@@ -121,6 +132,10 @@ def add_rms_norm(
     norm sees the float32 sum, not the rounded stored residual (reference
     ops.py:91-119).
     """
+    fp = _fast()
+    done = fp.add_rms_norm(x, residual, weight, eps, out, residual_out) if fp is not None else None
+    if done is not None:
+        return done
     _check_activation(x, "x")
     _check_activation(residual, "residual")
     _check_same(residual, x, "residual")
@@ -167,6 +182,10 @@ def rope(
     ``cos`` and ``sin`` broadcast over the leading dimensions (reference
     ops.py:138-160).
     """
+    fp = _fast()
+    done = fp.rope(x, cos, sin, out) if fp is not None else None
+    if done is not None:
+        return done
     _check_activation(x, "x")
     if x.shape[-1] % 2 != 0:
         raise ValueError("rope last dimension must be even")
@@ -188,6 +207,10 @@ def swiglu(
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``silu(gate) * up``: same shape, float32 math, stored in ``gate.dtype``."""
+    fp = _fast()
+    done = fp.swiglu(gate, up, out) if fp is not None else None
+    if done is not None:
+        return done
     _check_activation(gate, "gate")
     _check_activation(up, "up")
     _check_same(up, gate, "up")
@@ -251,6 +274,10 @@ def linear_decode(
     16 rows run the stream-K GEMV; wider batches pass through to ``F.linear``
     (reference ops.py:212-280).
     """
+    fp = _fast()
+    done = fp.linear_decode(x, weight, bias, row_add, out, kind) if fp is not None else None
+    if done is not None:
+        return done
     _check_activation(x, "x")
     if weight.ndim != 2:
         raise ValueError(f"weight must have shape [N, K], got {tuple(weight.shape)}")
@@ -315,6 +342,10 @@ def post_attn_mlp(
     run as two fused kernels (norm + gate/up GEMV + SwiGLU, then down GEMV +
     residual); other layouts run the four separate operators.
     """
+    fp = _fast()
+    done = fp.post_attn_mlp(hidden, norm_weight, w_gate_up, w_down, eps, kind) if fp is not None else None
+    if done is not None:
+        return done
     _check_activation(hidden, "hidden")
     if w_gate_up.ndim != 2 or w_down.ndim != 2:
         raise ValueError("w_gate_up and w_down must be rank-2")
