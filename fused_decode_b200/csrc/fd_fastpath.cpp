@@ -22,6 +22,7 @@
 #include <ATen/ops/zeros.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <ATen/PythonTorchFunctionTLS.h>
 #include <torch/csrc/autograd/python_variable.h>
 #include <torch/csrc/utils/pybind.h>
 
@@ -42,10 +43,21 @@ namespace {
 constexpr int64_t kMaxM = 16;  // GEMV batch rows (kernels.GEMV_MAX_M)
 
 // ------------------------------------------------------------ argument probes
-// A borrowed at::Tensor from a Python object, or nullptr when it is not one.
+// torch.Tensor and torch.nn.Parameter (which disables __torch_function__),
+// looked up when the module is imported.
+PyTypeObject* g_tensor_type = nullptr;
+PyTypeObject* g_parameter_type = nullptr;
+
+// A borrowed at::Tensor from a Python object, or nullptr when it is not one
+// or must go through Python: any other Tensor subclass (it may override
+// __torch_function__), any tensor while a torch-function mode is active
+// (e.g. `with torch.device(...)`), or a tensor without storage.
 const at::Tensor* as_tensor(py::handle h) {
-  if (!THPVariable_Check(h.ptr())) return nullptr;
-  return &THPVariable_Unpack(h.ptr());
+  const PyTypeObject* type = Py_TYPE(h.ptr());
+  if (type != g_tensor_type && type != g_parameter_type) return nullptr;
+  if (at::impl::torch_function_mode_enabled()) return nullptr;
+  const at::Tensor& t = THPVariable_Unpack(h.ptr());
+  return t.has_storage() ? &t : nullptr;
 }
 
 bool as_float(py::handle h, double* v) {
@@ -423,6 +435,10 @@ void clear_workspaces() {
 
 PYBIND11_MODULE(_fastpath, mod) {
   mod.doc() = "Compiled common-case dispatch of the fused_decode_b200 operators (None = use the Python path)";
+  // module-lifetime references (never released: the types outlive the module)
+  g_tensor_type = reinterpret_cast<PyTypeObject*>(py::object(py::module_::import("torch").attr("Tensor")).release().ptr());
+  g_parameter_type =
+      reinterpret_cast<PyTypeObject*>(py::object(py::module_::import("torch.nn").attr("Parameter")).release().ptr());
   mod.def("rms_norm", &rms_norm);
   mod.def("add_rms_norm", &add_rms_norm);
   mod.def("rope", &rope);

@@ -177,3 +177,20 @@ def test_linear_wide_batch_passes_through(fp):
     # forms the pass-through leaves to the Python path
     assert fp.linear_decode(x, w, b.float(), None, None, None) is None
     assert fp.linear_decode(x, w, None, torch.zeros(256, device="cuda", dtype=BF16), None, None) is None
+
+
+def test_parameters_subclasses_and_modes(fp):
+    g = _gen(9)
+    x = torch.randn(3, 256, device="cuda", dtype=F16, generator=g)
+    w = torch.nn.Parameter(torch.randn(256, device="cuda", dtype=F16, generator=g), requires_grad=False)
+    y = fp.rms_norm(x, w, 1e-6, None)  # model weights are Parameters: fast path
+    assert y is not None
+
+    class Tagged(torch.Tensor):
+        pass
+
+    assert fp.rms_norm(x.as_subclass(Tagged), w, 1e-6, None) is None
+    assert torch.equal(fd.rms_norm(x.as_subclass(Tagged), w).as_subclass(torch.Tensor), y)
+    with torch.device("cuda"):  # a torch-function mode: declined, computed by the Python path
+        assert fp.rms_norm(x, w, 1e-6, None) is None
+        assert torch.equal(fd.rms_norm(x, w), y)
