@@ -239,41 +239,109 @@ def _compile_into(row: dict, eager, mode: str, ours_us: float, iters: int) -> No
         row[f"compile_{mode}_error"] = f"{type(exc).__name__}: {exc}"
 
 
+# ------------------------------------------------------------------ the row plan
+# Shapes and row names of the table (the reference's, src/fused_decode/
+# bench.py:193-448).  The timing code below and row_names() both read these,
+# so the row set can be checked without a GPU.
+def norm_shapes(quick: bool) -> list[tuple[int, int]]:
+    return [(2048, LLAMA_H), (1, LLAMA_H)] if quick else [(8192, LLAMA_H), (2048, LLAMA_H), (1, LLAMA_H)]
+
+
+def swiglu_rows(quick: bool) -> tuple[int, ...]:
+    return (2048,) if quick else (1, 2048)
+
+
+def rope_cases(quick: bool) -> list[tuple[tuple[int, ...], tuple[int, ...]]]:
+    """(x shape, cos/sin shape): cos/sin broadcast over heads as [S, 1, D]."""
+    return [((1, 2048, 32, 128), (2048, 1, 128))] + ([] if quick else [((1, 1, 32, 128), (1, 1, 128))])
+
+
+def linear_shapes(quick: bool) -> list[tuple[int, int, int]]:
+    h, i = LLAMA_H, LLAMA_I
+    if quick:
+        return [(1, h, h), (8, h, h), (32, h, h)]
+    return [(1, h, h), (1, h, i), (1, i, h), (4, h, h), (8, h, h), (16, h, h), (32, h, h), (128, h, h)]
+
+
+def linear_kinds(m: int) -> tuple[str, ...]:
+    """Kinds timed per shape: both GEMV kinds up to the GEMV's batch limit."""
+    return ("dot", "simt") if m <= fd.DECODE_LINEAR_MAX_M else ()
+
+
+def mlp_cases(quick: bool) -> list[tuple[int, tuple]]:
+    """(batch rows, kinds); kind None is the default dispatcher."""
+    return [(1, (None, "simt"))] + ([] if quick else [(8, (None,))])
+
+
+def name_norm(op: str, rows_n: int, h: int, dtype) -> str:
+    return f"{op} {rows_n}x{h} {dtype}"
+
+
+def name_swiglu(rows_n: int, dtype) -> str:
+    return f"swiglu {rows_n}x{LLAMA_I} {dtype}"
+
+
+def name_rope(xs, dtype) -> str:
+    return f"rope {tuple(xs)} {dtype}"
+
+
+def name_linear(m: int, n: int, k: int, kind: str, dtype) -> str:
+    return f"linear M={m} N={n} K={k} {kind} {dtype}"
+
+
+def name_mlp(m: int, kind, dtype) -> str:
+    return f"post_attn_mlp M={m} {'default' if kind is None else kind} {dtype}"
+
+
+def row_names(dtype, quick: bool = False) -> list[str]:
+    """The rows one dtype contributes, in the order the table writes them."""
+    names = []
+    for rows_n, h in norm_shapes(quick):
+        names += [name_norm("rms_norm", rows_n, h, dtype), name_norm("add_rms_norm", rows_n, h, dtype)]
+    names += [name_swiglu(rows_n, dtype) for rows_n in swiglu_rows(quick)]
+    names += [name_rope(xs, dtype) for xs, _ in rope_cases(quick)]
+    for m, n, k in linear_shapes(quick):
+        if m > 1:
+            names.append(name_linear(m, n, k, "dispatch", dtype))
+        names += [name_linear(m, n, k, kind, dtype) for kind in linear_kinds(m)]
+    for m, kinds in mlp_cases(quick):
+        names += [name_mlp(m, kind, dtype) for kind in kinds]
+    return names
+
+
 def bench_rows_ops(t: Table, dtype: torch.dtype, quick: bool) -> None:
     """RMSNorm, add+RMSNorm, SwiGLU and RoPE at the reference's bench shapes
     (src/fused_decode/bench.py:193-300)."""
     item = torch.empty((), dtype=dtype).element_size()
-    shapes = [(2048, LLAMA_H), (1, LLAMA_H)] if quick else [(8192, LLAMA_H), (2048, LLAMA_H), (1, LLAMA_H)]
-    for rows_n, h in shapes:
+    for rows_n, h in norm_shapes(quick):
         x = torch.randn(rows_n, h, device="cuda", dtype=dtype)
         res = torch.randn_like(x)
         w = torch.randn(h, device="cuda", dtype=dtype)
         t.pointwise(
-            f"rms_norm {rows_n}x{h} {dtype}",
+            name_norm("rms_norm", rows_n, h, dtype),
             lambda: fd.rms_norm(x, w), lambda: F.rms_norm(x, (h,), w, 1e-6),
             (2 * rows_n * h + h) * item,
             checks={"max_abs": lambda: _max_abs(fd.rms_norm(x, w), F.rms_norm(x, (h,), w, 1e-6)),
                     "max_abs_vs_fp32": lambda: _max_abs(fd.rms_norm(x, w), R.rms_norm_reference(x, w))},
         )
         t.pointwise(
-            f"add_rms_norm {rows_n}x{h} {dtype}",
+            name_norm("add_rms_norm", rows_n, h, dtype),
             lambda: fd.add_rms_norm(x, res, w), lambda: F.rms_norm(x + res, (h,), w, 1e-6),
             (4 * rows_n * h + h) * item,
             checks={"max_abs_vs_fp32": lambda: max(
                 _max_abs(a, b) for a, b in zip(fd.add_rms_norm(x, res, w), R.add_rms_norm_reference(x, res, w)))},
             compile_this=dtype == torch.float16 and rows_n == 2048,
         )
-    for rows_n in ((2048,) if quick else (1, 2048)):
+    for rows_n in swiglu_rows(quick):
         g = torch.randn(rows_n, LLAMA_I, device="cuda", dtype=dtype)
         u = torch.randn_like(g)
         t.pointwise(
-            f"swiglu {rows_n}x{LLAMA_I} {dtype}",
+            name_swiglu(rows_n, dtype),
             lambda: fd.swiglu(g, u), lambda: F.silu(g) * u, 3 * g.numel() * item,
             checks={"max_abs_vs_fp32": lambda: _max_abs(fd.swiglu(g, u), R.swiglu_reference(g, u))},
             compile_this=dtype == torch.float16 and rows_n == 2048,
         )
-    rope_shapes = [((1, 2048, 32, 128), (2048, 1, 128))] + ([] if quick else [((1, 1, 32, 128), (1, 1, 128))])
-    for xs, cs in rope_shapes:
+    for xs, cs in rope_cases(quick):
         x = torch.randn(*xs, device="cuda", dtype=dtype)
         cos = torch.randn(*cs, device="cuda", dtype=dtype)
         sin = torch.randn(*cs, device="cuda", dtype=dtype)
@@ -286,7 +354,7 @@ def bench_rows_ops(t: Table, dtype: torch.dtype, quick: bool) -> None:
             return torch.cat((x1 * c1 - x2 * s1, x2 * c2 + x1 * s2), dim=-1)
 
         t.pointwise(
-            f"rope {tuple(xs)} {dtype}",
+            name_rope(xs, dtype),
             lambda: fd.rope(x, cos, sin), eager, 2 * x.nbytes + cos.nbytes + sin.nbytes,
             checks={"max_abs": lambda: _max_abs(fd.rope(x, cos, sin), R.rope_reference(x, cos, sin))},
             compile_this=dtype == torch.float16 and xs[1] == 2048,
@@ -300,11 +368,8 @@ def bench_rows_linear(t: Table, dtype: torch.dtype, quick: bool) -> None:
     Issued flops count the batch columns the tensor-core path computes: the
     ``dot`` consumers run m16n8k16 with the batch as the 8-wide operand, so
     M<=8 issues 8 columns and M<=16 issues 16; ``simt`` issues M."""
-    h, i = LLAMA_H, LLAMA_I
-    shapes = ([(1, h, h), (8, h, h), (32, h, h)] if quick else
-              [(1, h, h), (1, h, i), (1, i, h), (4, h, h), (8, h, h), (16, h, h), (32, h, h), (128, h, h)])
     item = torch.empty((), dtype=dtype).element_size()
-    for m, n, k in shapes:
+    for m, n, k in linear_shapes(quick):
         x = torch.randn(m, k, device="cuda", dtype=dtype) * k**-0.5
         w = torch.randn(n, k, device="cuda", dtype=dtype) * k**-0.5
         nbytes = (m * k + n * k + m * n) * item
@@ -313,21 +378,21 @@ def bench_rows_linear(t: Table, dtype: torch.dtype, quick: bool) -> None:
         if m > 1:
             us = time_us(lambda: fd.linear_decode(x, w), iters=30, warmup=5, rounds=3)
             t.add({
-                "name": f"linear M={m} N={n} K={k} dispatch {dtype}", "us": us, "eager_us": eager_us,
+                "name": name_linear(m, n, k, "dispatch", dtype), "us": us, "eager_us": eager_us,
                 "mv_us": mv_us, "speedup_vs_eager": _speedup(eager_us, us), "bytes": nbytes,
                 "note": (f"default dispatcher: hand-written GEMV up to M={fd.DECODE_LINEAR_MAX_M}, "
                          "cuBLAS above"),
             })
-        if m > fd.DECODE_LINEAR_MAX_M:
+        if not linear_kinds(m):
             continue
         ref = R.linear_reference(x, w)
         cublas = F.linear(x, w)
-        for kind in ("dot", "simt"):
+        for kind in linear_kinds(m):
             us = time_us(lambda: fd.linear_decode(x, w, kind=kind), iters=50)
             ours = fd.linear_decode(x, w, kind=kind)
             cols = (8 if m <= 8 else 16) if kind == "dot" else m
             issued = 2.0 * cols * n * k / us / 1e6
-            row = {"name": f"linear M={m} N={n} K={k} {kind} {dtype}", "us": us, "eager_us": eager_us,
+            row = {"name": name_linear(m, n, k, kind, dtype), "us": us, "eager_us": eager_us,
                    "mv_us": mv_us, "speedup_vs_eager": _speedup(eager_us, us),
                    "speedup_vs_mv": _speedup(mv_us, us)}
             row.update(t.bandwidth(nbytes, us))
@@ -358,7 +423,7 @@ def bench_rows_mlp(t: Table, dtype: torch.dtype, quick: bool) -> None:
     formulation (src/fused_decode/bench.py:388-448), plus two graph times:
     the reference's (one weight set, L2-warm) and one with the weights rotated
     across copies that together exceed L2, which is what a layer stack sees."""
-    for m in ((1,) if quick else (1, 8)):
+    for m, kinds in mlp_cases(quick):
         hidden, norm_w, sets = _mlp_weights(dtype, m, copies=2)
         w_gu, w_dn = sets[0]
 
@@ -367,7 +432,7 @@ def bench_rows_mlp(t: Table, dtype: torch.dtype, quick: bool) -> None:
             gate, up = F.linear(hh, w_gu).split(LLAMA_I, dim=-1)
             return F.linear(F.silu(gate) * up, w_dn) + hidden
 
-        for kind in ((None, "simt") if m == 1 else (None,)):
+        for kind in kinds:
             def ours(w_gu=w_gu, w_dn=w_dn, kind=kind):
                 return fd.post_attn_mlp(hidden, norm_w, w_gu, w_dn, kind=kind)
 
@@ -375,7 +440,7 @@ def bench_rows_mlp(t: Table, dtype: torch.dtype, quick: bool) -> None:
             eager_us = time_us(eager, iters=30, warmup=10)
             with torch.no_grad():
                 got = ours()
-                row = {"name": f"post_attn_mlp M={m} {'default' if kind is None else kind} {dtype}",
+                row = {"name": name_mlp(m, kind, dtype),
                        "us": us, "eager_us": eager_us, "speedup_vs_eager": _speedup(eager_us, us),
                        "max_abs_vs_eager": _max_abs(got, eager()),
                        "max_abs_vs_fp32": _max_abs(got, R.post_attn_mlp_reference(hidden, norm_w, w_gu, w_dn))}
