@@ -280,6 +280,23 @@ bool row_add_strides(const at::Tensor& ra, int64_t m, int64_t n, c10::IntArrayRe
   return false;
 }
 
+// x as [M, K] without a copy (ops._as_mk): 2-D with non-negative strides as
+// it is, or contiguous of any rank viewed as [-1, K]; else not on the fast path.
+bool as_mk(const at::Tensor& x, int64_t* m, int64_t* sxm, int64_t* sxk) {
+  const int64_t k = x.size(-1);
+  if (x.dim() == 2 && x.stride(0) >= 0 && x.stride(1) >= 0) {
+    *m = x.size(0);
+    *sxm = x.stride(0);
+    *sxk = x.stride(1);
+    return true;
+  }
+  if (!x.is_contiguous()) return false;
+  *m = k == 0 ? 0 : x.numel() / k;
+  *sxm = k;
+  *sxk = 1;
+  return true;
+}
+
 py::object linear_decode(py::handle hx, py::handle hw, py::handle hb, py::handle hra, py::handle hout,
                          py::handle hkind) {
   const at::Tensor* x = as_tensor(hx);
@@ -290,20 +307,8 @@ py::object linear_decode(py::handle hx, py::handle hw, py::handle hb, py::handle
     return py::none();
   const int64_t n = w->size(0), k = w->size(1);
   if (x->size(-1) != k) return py::none();
-  // x as [M, K] without a copy: 2-D with non-negative strides as it is, or
-  // contiguous of any rank viewed as [-1, K] (ops._as_mk)
   int64_t sxm, sxk, m;
-  if (x->dim() == 2 && x->stride(0) >= 0 && x->stride(1) >= 0) {
-    m = x->size(0);
-    sxm = x->stride(0);
-    sxk = x->stride(1);
-  } else if (x->is_contiguous()) {
-    m = k == 0 ? 0 : x->numel() / k;
-    sxm = k;
-    sxk = 1;
-  } else {
-    return py::none();
-  }
+  if (!as_mk(*x, &m, &sxm, &sxk)) return py::none();
   if (m < 1 || n < 1 || k < 1) return py::none();
   std::vector<int64_t> expected(x->sizes().begin(), x->sizes().end() - 1);
   expected.push_back(n);
@@ -413,6 +418,31 @@ py::object post_attn_mlp(py::handle hh, py::handle hnw, py::handle hgu, py::hand
   return py::cast(out);
 }
 
+// ------------------------------------------------------------ test hooks
+// The arguments the fast path derives from a tensor's layout, for any device,
+// so tests can compare them with the Python path's without a GPU.
+py::object layout_rows(py::handle h) {
+  const at::Tensor* t = as_tensor(h);
+  fd_rows r;
+  if (!t || !rows_of(*t, &r)) return py::none();
+  return py::make_tuple(r.a, r.b, r.c, r.sa, r.sb, r.sc, r.col, r.n);
+}
+
+// (m, sxm, sxk, srm, srn) for x [..., K] against an [n, K] weight and an
+// optional row_add, or None where the fast path would decline.
+py::object layout_linear(py::handle hx, int64_t n, py::handle hra) {
+  const at::Tensor* x = as_tensor(hx);
+  int64_t m, sxm, sxk, srm = 0, srn = 0;
+  if (!x || x->dim() < 1 || !as_mk(*x, &m, &sxm, &sxk)) return py::none();
+  if (!hra.is_none()) {
+    std::vector<int64_t> expected(x->sizes().begin(), x->sizes().end() - 1);
+    expected.push_back(n);
+    const at::Tensor* ra = as_tensor(hra);
+    if (!ra || !row_add_strides(*ra, m, n, expected, &srm, &srn)) return py::none();
+  }
+  return py::make_tuple(m, sxm, sxk, srm, srn);
+}
+
 // ------------------------------------------------------------ workspace API
 at::Tensor workspace(int64_t device, int64_t nbytes) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
@@ -445,6 +475,8 @@ PYBIND11_MODULE(_fastpath, mod) {
   mod.def("swiglu", &swiglu);
   mod.def("linear_decode", &linear_decode);
   mod.def("post_attn_mlp", &post_attn_mlp);
+  mod.def("layout_rows", &layout_rows);
+  mod.def("layout_linear", &layout_linear);
   mod.def("workspace", &workspace);
   mod.def("workspaces", &workspaces);
   mod.def("clear_workspaces", &clear_workspaces);
