@@ -1,8 +1,10 @@
-"""ctypes binding of the C ABI in ``include/fd_b200.h`` (``libfd_b200.so``).
+"""ctypes binding of the C ABI in ``include/fd_b200.h`` (``libfd_b200.so``),
+and the loader of the compiled dispatch module ``_fastpath`` that calls the
+same entry points from C++.
 
-This is the only place Python touches the native library.  Loading fails
-loudly when the shared library has not been built: there is no CPU or
-PyTorch fallback behind these entry points.
+These are the only places Python reaches the native code.  Loading fails
+loudly when either has not been built: there is no CPU or PyTorch fallback
+behind these entry points.
 """
 
 from __future__ import annotations
