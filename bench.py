@@ -27,7 +27,6 @@ import sys
 import threading
 import time
 
-import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -35,7 +34,8 @@ sys.path.insert(0, ROOT)
 H, I = 4096, 14336
 LAYERS = 32
 EPS = 1e-5
-PUBLISHED_US = {1: 1570.0, 8: 1621.0}  # reference bf16 post_attn_mlp, RTX 4070 Laptop
+# The reference's published bf16 post_attn_mlp times, RTX 4070 Laptop (its results/rtx4070-laptop.json:813,829)
+PUBLISHED_US = {1: 1570.0, 8: 1621.0}
 METRIC = "post_attn_mlp us/layer at M=1 (Llama-3-8B widths, 32-layer CUDA graph), HBM GB/s vs measured peak"
 
 
@@ -74,20 +74,33 @@ def committed_traffic() -> dict:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region.
+
+    NVML is polled every ~10 ms from a thread (a 40 ms timed region still
+    gets several samples); where NVML cannot be opened, ``nvidia-smi -lms 100``
+    is read instead.  The GPU is found by its UUID, so CUDA_VISIBLE_DEVICES
+    renumbering does not matter.  Reading clocks changes no GPU setting.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int) -> None:
+    def __init__(self, gpu_index: int, uuid: str | None = None) -> None:
         self.gpu = gpu_index
-        self.lines: list[tuple[float, str]] = []
+        self.uuid = uuid
+        self.samples: list[tuple[float, float, float, set]] = []  # (t, sm MHz, max MHz, reasons)
         self.proc = None
         self.thread = None
         self.window = None
+        self.source = None
+        self._stop = threading.Event()
 
     def start(self) -> None:
+        if self._start_nvml():
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -96,90 +109,143 @@ class ClockSampler:
         except OSError:
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.source = "nvidia-smi -lms 100"
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
         time.sleep(0.3)
 
-    def _read(self) -> None:
+    def _start_nvml(self) -> bool:
+        try:
+            import pynvml as N
+
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid else N.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+            N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+        except Exception:
+            return False
+        self.source = "nvml every 10 ms"
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    sm = float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM))
+                    bits = int(N.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except Exception:
+                    break
+                self.samples.append((time.perf_counter(), sm, mx,
+                                     {name for name, bit in self.REASONS if bits & bit}))
+                time.sleep(0.01)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        time.sleep(0.05)
+        return True
+
+    def _read_smi(self) -> None:
         for line in self.proc.stdout:
-            self.lines.append((time.perf_counter(), line.strip()))
+            parts = [p.strip() for p in line.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            names = [n for n, _ in self.REASONS]
+            self.samples.append((time.perf_counter(), sm, mx,
+                                 {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
 
     def mark(self, t0: float, t1: float) -> None:
         """Restrict the summary to samples taken in [t0, t1] (the timed region)."""
         self.window = (t0, t1)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        lines = self.lines
+        if self.source is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
+        samples = self.samples
         if self.window is not None:
-            inside = [ln for t, ln in lines if self.window[0] <= t <= self.window[1] + 0.15]
-            lines = inside if inside else [ln for _, ln in lines]
-        else:
-            lines = [ln for _, ln in lines]
-        for ln in lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+            slack = 0.15 if self.proc is not None else 0.0
+            inside = [x for x in samples if self.window[0] <= x[0] <= self.window[1] + slack]
+            samples = inside or samples
+        reasons = set().union(*(x[3] for x in samples)) if samples else set()
+        return {"sm_mhz": statistics.median(x[1] for x in samples) if samples else None,
+                "sm_max_mhz": max(x[2] for x in samples) if samples else None,
+                "reasons": sorted(reasons), "samples": len(samples), "source": self.source}
+
+
+def gpu_uuid(torch, device) -> str | None:
+    try:
+        u = str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        return None
+    return u if u.startswith("GPU-") else "GPU-" + u
 
 
 # ------------------------------------------------------------------ CPU leg
-def cpu_layer_sample(layers: int, m: int, seed: int = 0):
-    """Seeded fp32 copies (bf16-rounded values) of `layers` Llama-3-8B MLP layers for the CPU leg."""
-    from oracle import fd_oracle as O
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    rng = np.random.default_rng(seed)
+
+def cpu_layer_sample(layers: int, m: int, seed: int = 0):
+    """Seeded bf16 CPU tensors for `layers` Llama-3-8B MLP layers and an [m, H] hidden state."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
     out = []
     for _ in range(layers):
-        nw = O.round_bf16(1 + 0.1 * rng.standard_normal(H, dtype=np.float32))
-        wgu = O.round_bf16(rng.standard_normal((2 * I, H), dtype=np.float32) * np.float32(0.02))
-        wd = O.round_bf16(rng.standard_normal((H, I), dtype=np.float32) * np.float32(0.02))
+        nw = (1 + 0.1 * torch.randn(H, generator=g)).to(bf)
+        wgu = (torch.randn(2 * I, H, generator=g) * 0.02).to(bf)
+        wd = (torch.randn(H, I, generator=g) * 0.02).to(bf)
         out.append((nw, wgu, wd))
-    x = O.round_bf16(rng.standard_normal((m, H), dtype=np.float32))
-    return x, out
+    return torch.randn(m, H, generator=g).to(bf), out
 
 
-def cpu_time_layers(x, layers, budget_s: float, min_evals: int, max_evals: int | None = None):
-    """Time the oracle's post_attn_mlp per layer; returns (us/layer, evals, threads)."""
-    from oracle import fd_oracle as O
+def cpu_time_layers(x, layers, warmup: int, evals: int):
+    """Median wall time (us) of one post_attn_mlp layer of the reference's
+    PyTorch-eager CPU formulation on all host cores; returns (us, evals, threads)."""
+    import torch
 
-    try:
-        from threadpoolctl import threadpool_info, threadpool_limits
+    from oracle import fd_oracle_torch as T
 
-        threadpool_limits(os.cpu_count())
-        threads = max((d.get("num_threads", 1) for d in threadpool_info()), default=1)
-    except Exception:  # threadpoolctl missing: BLAS picks its own count
-        threads = os.cpu_count()
+    torch.set_num_threads(os.cpu_count() or 1)
     times = []
-    t_end = time.perf_counter() + budget_s
-    j = 0
-    while (len(times) < min_evals or time.perf_counter() < t_end) and (max_evals is None or len(times) < max_evals):
+    for j in range(warmup + evals):
         nw, wgu, wd = layers[j % len(layers)]
         t0 = time.perf_counter()
-        x = O.post_attn_mlp(x, nw, wgu, wd, EPS, O.BF16)
-        times.append(time.perf_counter() - t0)
-        j += 1
-    return statistics.median(times) * 1e6, len(times), threads
+        x = T.post_attn_mlp(x, nw, wgu, wd, EPS)
+        if j >= warmup:
+            times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6, len(times), torch.get_num_threads()
+
+
+def cpu_baseline(m: int, warmup: int, evals: int) -> dict:
+    """The CPU baseline both arms report: the reference's PyTorch-eager CPU path
+    (reference.py:66-79, restated in oracle/fd_oracle_torch.py) timed layer by layer."""
+    x, layers = cpu_layer_sample(2, m)
+    us, n, threads = cpu_time_layers(x, layers, warmup, evals)
+    return {"value": us, "unit": "us/layer", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(), "os_cpu_count": os.cpu_count(),
+            "sample": (f"median of {n} single-layer evaluations (after {warmup} warm-up) alternating over 2 "
+                       f"seeded Llama-3-8B MLP layers, M={m}, bf16 tensors: the reference's PyTorch-eager CPU "
+                       f"formulation (fp32 F.linear on the CPU, its three rounding points) with "
+                       f"torch.set_num_threads({threads})")}
 
 
 def workload_config(m: int, world: int, collective: str) -> dict:
@@ -194,23 +260,21 @@ def workload_config(m: int, world: int, collective: str) -> dict:
 
 
 def run_reference(args) -> None:
-    """The reference arm: the reference's CPU formulation (oracle port) on host cores."""
+    """The reference arm: the reference's PyTorch-eager CPU path on the host
+    cores, each step one layer of the workload (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     m = args.m
-    x, layers = cpu_layer_sample(2, m)
-    cpu_time_layers(x, layers, 0.0, max(1, args.warmup), max(1, args.warmup))  # warm-up
-    us, evals, threads = cpu_time_layers(x, layers, 0.0, args.steps, args.steps)
-    sample = (f"{evals} single-layer steps over 2 seeded Llama-3-8B MLP layers, M={m}, numpy fp32 "
-              f"(oracle port of reference.py:66-79) on the host cores; each step is one layer of the workload")
+    cpu = cpu_baseline(m, max(1, args.warmup), args.steps)
+    us = cpu["value"]
     line = {
         "impl": "reference", "metric": METRIC, "value": us, "unit": "us/layer",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3,
-        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,0.02) weights rounded to bf16)",
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights in bf16)",
         "config": workload_config(m, args.gpus, args.tp_collective),
-        "cpu_baseline": {"value": us, "unit": "us/layer", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": cpu,
         "e2e": {"value": us, "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -299,20 +363,29 @@ def copies_for(nbytes: int) -> int:
 
 
 def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
-    """Standalone ops at the BASELINE shapes: us per call, algorithmic GB/s and
+    """Standalone ops at the benchmark configurations' shapes: us per call, algorithmic GB/s and
     fractions of the in-process copy roof and of the measured peak."""
     import fused_decode_b200 as fd
+    from fused_decode_b200 import reference as R
 
     g = torch.Generator(device=device).manual_seed(0)
     out: dict = {}
 
-    def rec(name, us, nbytes, **extra):
+    def rec(name, us, nbytes, check=None, **extra):
+        """One row; ``check()`` returns (output, fp32-formulation output) of one
+        call on the row's inputs: max_abs and the atol = rtol = 1e-2 verdict."""
         gbs = nbytes / (us * 1e-6) / 1e9
-        out[name] = {"us": us, "bytes": nbytes, "gbs": gbs, "frac_copy_roof": gbs / roof_gbs,
-                     "frac_peak": gbs / peak_gbs, **extra}
+        row = {"us": us, "bytes": nbytes, "gbs": gbs, "frac_copy_roof": gbs / roof_gbs,
+               "frac_peak": gbs / peak_gbs, **extra}
+        if check is not None:
+            got, want = check()
+            got, want = got.float(), want.to(got.device).float()
+            row["max_abs_vs_fp32_reference"] = float((got - want).abs().max()) if got.numel() else 0.0
+            row["parity_ok"] = bool(torch.allclose(got, want, rtol=1e-2, atol=1e-2))
+        out[name] = row
 
     f16 = torch.float16
-    # add+RMSNorm and RMSNorm (BASELINE config 0)
+    # add+RMSNorm and RMSNorm at [8192, 4096] and [1, 4096]
     for rows in (8192, 1):
         w = (1 + 0.1 * torch.randn(H, device=device, generator=g)).to(f16)
         n_add = 4 * rows * H * 2 + H * 2
@@ -320,12 +393,15 @@ def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
         xs = [torch.randn(rows, H, device=device, dtype=f16, generator=g) for _ in range(k)]
         rs = [torch.randn(rows, H, device=device, dtype=f16, generator=g) for _ in range(k)]
         os_ = [torch.empty(rows, H, device=device, dtype=f16) for _ in range(k)]
+        x_c, r_c = xs[0].clone(), rs[0].clone()  # the timed calls update rs in place
         calls = [(lambda j=j: fd.add_rms_norm(xs[j], rs[j], w, 1e-5, out=os_[j], residual_out=rs[j]))
                  for j in range(k)]
-        rec(f"add_rms_norm_{rows}x{H}_f16", graph_time_us(torch, calls), n_add)
+        rec(f"add_rms_norm_{rows}x{H}_f16", graph_time_us(torch, calls), n_add,
+            check=lambda: (fd.add_rms_norm(x_c, r_c, w, 1e-5)[0], R.add_rms_norm_reference(x_c, r_c, w, 1e-5)[0]))
         n_rms = 2 * rows * H * 2 + H * 2
         calls = [(lambda j=j: fd.rms_norm(xs[j], w, 1e-5, out=os_[j])) for j in range(k)]
-        rec(f"rms_norm_{rows}x{H}_f16", graph_time_us(torch, calls), n_rms)
+        rec(f"rms_norm_{rows}x{H}_f16", graph_time_us(torch, calls), n_rms,
+            check=lambda: (fd.rms_norm(x_c, w, 1e-5), R.rms_norm_reference(x_c, w, 1e-5)))
         del xs, rs, os_
     # SwiGLU (config 1)
     for rows in (2048, 1):
@@ -336,7 +412,8 @@ def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
             us_ = [torch.randn(rows, I, device=device, dtype=dt, generator=g) for _ in range(k)]
             os_ = [torch.empty(rows, I, device=device, dtype=dt) for _ in range(k)]
             calls = [(lambda j=j: fd.swiglu(gs[j], us_[j], out=os_[j])) for j in range(k)]
-            rec(f"swiglu_{rows}x{I}_{tag}", graph_time_us(torch, calls), nb)
+            rec(f"swiglu_{rows}x{I}_{tag}", graph_time_us(torch, calls), nb,
+                check=lambda: (fd.swiglu(gs[0], us_[0]), R.swiglu_reference(gs[0], us_[0])))
             del gs, us_, os_
     # RoPE (config 1): x [1, T, 32, 128], cos/sin [T, 1, 128] from theta = 500000
     for t in (2048, 1):
@@ -346,7 +423,8 @@ def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
         xs = [torch.randn(1, t, 32, 128, device=device, dtype=f16, generator=g) for _ in range(k)]
         os_ = [torch.empty_like(xs[0]) for _ in range(k)]
         calls = [(lambda j=j: fd.rope(xs[j], cos, sin, out=os_[j])) for j in range(k)]
-        rec(f"rope_1x{t}x32x128_f16", graph_time_us(torch, calls), nb)
+        rec(f"rope_1x{t}x32x128_f16", graph_time_us(torch, calls), nb,
+            check=lambda: (fd.rope(xs[0], cos, sin), R.rope_reference(xs[0], cos, sin)))
         del xs, os_
     # linear_decode sweep (config 2); weights rotate through >= 2x L2
     for dt, tag in ((torch.bfloat16, "bf16"), (f16, "f16")):
@@ -358,7 +436,8 @@ def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
                 y = torch.empty(m, n, device=device, dtype=dt)
                 calls = [(lambda j=j: fd.linear_decode(x, ws[j], out=y, kind="dot")) for j in range(k)]
                 nb = (m * kk + n * kk + m * n) * 2
-                rec(f"linear_decode_m{m}_n{n}_k{kk}_{tag}", graph_time_us(torch, calls), nb)
+                rec(f"linear_decode_m{m}_n{n}_k{kk}_{tag}", graph_time_us(torch, calls), nb,
+                    check=lambda: (fd.linear_decode(x, ws[0], kind="dot"), R.linear_reference(x, ws[0])))
             if n == 4096 and kk == 14336:  # the down projection with bias + row_add
                 for m in (1, 8):
                     x = torch.randn(m, kk, device=device, dtype=dt, generator=g)
@@ -368,10 +447,196 @@ def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
                     calls = [(lambda j=j: fd.linear_decode(x, ws[j], b, row_add=ra, out=y, kind="dot"))
                              for j in range(k)]
                     nb = (m * kk + n * kk + 2 * m * n + n) * 2
-                    rec(f"linear_decode_m{m}_n{n}_k{kk}_{tag}_bias_rowadd", graph_time_us(torch, calls), nb)
+                    rec(f"linear_decode_m{m}_n{n}_k{kk}_{tag}_bias_rowadd", graph_time_us(torch, calls), nb,
+                        check=lambda: (fd.linear_decode(x, ws[0], b, row_add=ra, kind="dot"),
+                                       R.linear_reference(x, ws[0], b, row_add=ra)))
             del ws
     torch.cuda.empty_cache()
     return out
+
+
+# ------------------------------------------------------------------ TP decode block, Llama-3-70B widths
+H70, I70, Q_HEADS, KV_HEADS, HEAD_DIM, LAYERS70 = 8192, 28672, 64, 8, 128, 80
+BLOCK_MS = (1, 4, 8)
+
+
+def block_layer_bytes(m: int, world: int) -> int:
+    """Algorithmic HBM bytes of one decode-block layer on one rank: the rank's
+    MLP weight shards once; add_rms_norm (x, residual in; out, residual_out;
+    weight); RoPE on the rank's q/k heads (in, out, cos, sin); the MLP's
+    hidden (read twice: norm and residual), output and norm weight.  The
+    cross-rank exchange is NVLink traffic, not counted here."""
+    mlp_w = 3 * I70 * H70 * 2 // world
+    add_norm = 4 * m * H70 * 2 + H70 * 2
+    heads = (Q_HEADS + KV_HEADS) // world
+    rope_b = 2 * m * heads * HEAD_DIM * 2 + 2 * 2 * m * HEAD_DIM * 2
+    mlp_act = 3 * m * H70 * 2 + H70 * 2
+    return mlp_w + add_norm + rope_b + mlp_act
+
+
+def run_tp_block(torch, device, world, rank, args, pk, barrier, max_over_ranks) -> dict:
+    """The tensor-parallel decode block at Llama-3-70B widths: per layer,
+    add_rms_norm of the attention output into the residual stream, RoPE on
+    this rank's q [M,1,64/T,128] and k [M,1,8/T,128], then the MLP with
+    gate/up column-sharded and down row-sharded and the partial-sum exchange
+    before the residual add.  80 layers per step in one CUDA graph.
+
+    Weights are random-init per rank shard, N(0, 0.02) in bf16, drawn on the
+    device (the values never leave it; parity at these widths is a test).
+    Reports us/step and us/layer at M in {1, 4, 8}, the per-GPU HBM fraction,
+    and at M=1 a split of a layer into its kernels and the exchange."""
+    import fused_decode_b200 as fd
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200 import tp
+
+    bf = torch.bfloat16
+    gi, di = 2 * I70 // world, I70 // world
+    qh, kh = Q_HEADS // world, KV_HEADS // world
+    g = torch.Generator(device=device).manual_seed(7000 + rank)
+    layers = []
+    for _ in range(LAYERS70):
+        attn_w = (1 + 0.1 * torch.randn(H70, device=device, generator=g)).to(bf)
+        mlp_w = (1 + 0.1 * torch.randn(H70, device=device, generator=g)).to(bf)
+        wgu = torch.randn(gi, H70, device=device, dtype=bf, generator=g).mul_(0.02)
+        wd = torch.randn(H70, di, device=device, dtype=bf, generator=g).mul_(0.02)
+        layers.append((attn_w, mlp_w, wgu, wd))
+    exchange = tp.TPExchange(H70, m_max=max(BLOCK_MS)) if world > 1 and args.tp_collective == "nvlink" else None
+    res: dict = {"hidden": H70, "intermediate": I70, "q_heads": Q_HEADS, "kv_heads": KV_HEADS,
+                 "head_dim": HEAD_DIM, "layers": LAYERS70, "tp_world": world,
+                 "collective": (args.tp_collective if world > 1 else None),
+                 "weights_gb_per_gpu": LAYERS70 * 3 * I70 * H70 * 2 / world / 1e9}
+
+    def capture(fn, x):
+        cur = torch.cuda.current_stream()
+        s = torch.cuda.Stream()
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            fn(x)  # sizes workspaces outside the capture
+        cur.wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            out = fn(x)
+        return graph, out
+
+    def time_graph(graph, steps):
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(s.elapsed_time(e) / steps) * 1e3  # us per replay
+
+    def mlp(h2, mlp_w, wgu, wd):
+        if world == 1:
+            return fd.post_attn_mlp(h2, mlp_w, wgu, wd, EPS, kind="dot")
+        return tp.TPPostAttnMlp(mlp_w, wgu, wd, EPS, kind="dot", exchange=exchange)(h2)
+
+    steps = max(args.steps, 10)
+    per_m = {}
+    for m in BLOCK_MS:
+        gm = torch.Generator(device=device).manual_seed(71 + m)
+        attn_out = torch.randn(m, H70, device=device, dtype=bf, generator=gm)
+        q = torch.randn(m, 1, qh, HEAD_DIM, device=device, dtype=bf, generator=gm)
+        k = torch.randn(m, 1, kh, HEAD_DIM, device=device, dtype=bf, generator=gm)
+        q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+        pos = torch.arange(m, device=device, dtype=torch.float32) + 1000.0
+        inv = 500000.0 ** (-torch.arange(0, HEAD_DIM, 2, dtype=torch.float32, device=device) / HEAD_DIM)
+        f = torch.outer(pos, inv)
+        emb = torch.cat((f, f), dim=-1)
+        cos, sin = emb.cos().to(bf).view(m, 1, 1, HEAD_DIM), emb.sin().to(bf).view(m, 1, 1, HEAD_DIM)
+        x0 = torch.randn(m, H70, device=device, dtype=bf, generator=gm)
+
+        def block(x, attn_out=attn_out, q=q, k=k, q_out=q_out, k_out=k_out, cos=cos, sin=sin):
+            h = x
+            for attn_w, mlp_w, wgu, wd in layers:
+                _, h2 = fd.add_rms_norm(attn_out, h, attn_w, EPS)
+                fd.rope(q, cos, sin, out=q_out)
+                fd.rope(k, cos, sin, out=k_out)
+                h = mlp(h2, mlp_w, wgu, wd)
+            return h
+
+        graph, _ = capture(block, x0)
+        us = time_graph(graph, steps)
+        del graph
+        nb = block_layer_bytes(m, world)
+        gbs = nb * LAYERS70 / (us * 1e-6) / 1e9
+        per_m[f"m{m}"] = {"us_per_step": us, "us_per_layer": us / LAYERS70, "bytes_per_layer_per_gpu": nb,
+                          "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / pk["hbm_gbs"]}
+
+        if m == 1:
+            # the same layer's pieces, each as 80 launches in one graph
+            part = torch.empty(m, H70, device=device, dtype=torch.float32)
+            mid = torch.empty(m, di, device=device, dtype=bf)
+
+            def local_only(x, attn_out=attn_out, q=q, k=k, q_out=q_out, k_out=k_out, cos=cos, sin=sin):
+                h = x
+                for attn_w, mlp_w, wgu, wd in layers:  # every kernel of the layer, no cross-rank sum
+                    _, h2 = fd.add_rms_norm(attn_out, h, attn_w, EPS)
+                    fd.rope(q, cos, sin, out=q_out)
+                    fd.rope(k, cos, sin, out=k_out)
+                    K.post_attn_mlp_out(h2, mlp_w, wgu, wd, part, EPS, "dot", add_residual=False)
+                    h = h2
+                return h
+
+            def gate_up(x):
+                for _, mlp_w, wgu, _ in layers:
+                    K.mlp_gate_up_out(x, mlp_w, wgu, mid, EPS, "dot")
+                return mid
+
+            y_dn = torch.empty(m, H70, device=device, dtype=bf)
+
+            def down(x):
+                for _, _, _, wd in layers:  # bf16 output instead of the fp32 partial: 16 KB less store
+                    K.linear_out(mid, wd, y_dn, kind="dot")
+                return y_dn
+
+            def elementwise(x, attn_out=attn_out, q=q, k=k, q_out=q_out, k_out=k_out, cos=cos, sin=sin):
+                h = x
+                for attn_w, _, _, _ in layers:
+                    _, h = fd.add_rms_norm(attn_out, h, attn_w, EPS)
+                    fd.rope(q, cos, sin, out=q_out)
+                    fd.rope(k, cos, sin, out=k_out)
+                return h
+
+            split = {}
+            for name, fn in (("local_layer_no_exchange", local_only), ("gate_up", gate_up), ("down", down),
+                             ("add_rms_norm_and_rope", elementwise)):
+                graph, _ = capture(fn, x0)
+                split[name] = time_graph(graph, steps) / LAYERS70
+                del graph
+            split["exchange_and_residual"] = (per_m["m1"]["us_per_layer"] - split["local_layer_no_exchange"]
+                                              if world > 1 else 0.0)
+            res["split_us_per_layer_m1"] = split
+            if world > 1:
+                import torch.distributed as dist
+
+                buf = torch.zeros(m, H70, device=device, dtype=torch.float32)
+
+                def allreduce(x):
+                    for _ in range(LAYERS70):
+                        dist.all_reduce(buf)
+                    return buf
+
+                graph, _ = capture(allreduce, x0)
+                res["nccl_allreduce_us_m1"] = time_graph(graph, steps) / LAYERS70
+                del graph
+        del attn_out, q, k, q_out, k_out
+    res["per_m"] = per_m
+    res["us_per_step"] = per_m["m1"]["us_per_step"]
+    res["us_per_layer"] = per_m["m1"]["us_per_layer"]
+    torch.cuda.synchronize()
+    if exchange is not None:
+        exchange.close()
+    del layers
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_ours(args) -> None:
@@ -563,15 +828,10 @@ def run_ours(args) -> None:
     e2e_s = wall(e2e_graph_step, args.steps)
     e2e_eager_s = wall(e2e_eager_step, max(3, args.steps // 10))
 
-    # ---- CPU baseline (rank 0, N=1 only): oracle port, bounded sample
+    # ---- CPU baseline (rank 0, N=1 only): the reference's PyTorch-eager CPU path, bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        xs, cl = cpu_layer_sample(2, args.m)
-        cpu_time_layers(xs, cl, 0.0, 1, 1)
-        us_cpu, evals, threads = cpu_time_layers(xs, cl, args.cpu_seconds, 3)
-        cpu = {"value": us_cpu, "unit": "us/layer", "cores": threads, "kind": "port",
-               "sample": f"{evals} layer evaluations over 2 seeded Llama-3-8B MLP layers at M={args.m} "
-                         f"(numpy fp32 oracle port of reference.py:66-79), ~{args.cpu_seconds:.0f} s"}
+        cpu = cpu_baseline(args.m, 2, args.cpu_evals)
 
     ops = None
     if world == 1 and not args.no_ops:
@@ -708,7 +968,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--m", type=int, default=1)
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-evals", type=int, default=20, help="timed CPU-baseline layer evaluations")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="skip the standalone-op measurements")
     ap.add_argument("--tp-collective", choices=("nvlink", "nccl"), default="nvlink",

@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple] = {
         ],
     ),
     "fd_linear_noalloc_scratch_bytes": (c_size, []),
+    "fd_linear_noalloc_status": (c_i32, [ctypes.POINTER(c_i32), c_vp]),
+    "fd_linear_noalloc_reset": (c_i32, [c_vp]),
     "fd_linear_out_noalloc": (
         c_i32,
         [

@@ -490,4 +490,34 @@ int fd_linear_out_noalloc(const void* x, int64_t sxm, int64_t sxk, const void* w
                        dtype, m, n, k, kind, scratch, kNoAllocScratchBytes, stream);
 }
 
+// The scratch's status word, after every call enqueued on `stream` so far:
+// non-zero when a bounded in-kernel wait expired (the bits of the workspace
+// status word).  Copies 4 bytes into host memory and waits for `stream`.
+int fd_linear_noalloc_status(int32_t* status, void* stream) {
+  if (!status) return FD_ERR_ARG;
+  void* scratch = nullptr;
+  const int r = noalloc_scratch(&scratch);
+  if (r != FD_OK) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, static_cast<char*>(scratch) + status_offset(), sizeof(v), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return FD_ERR_DEVICE;
+  *status = v;
+  return FD_OK;
+}
+
+// Zero the scratch's split-K counters and status word on `stream`: the state
+// a launch needs.  After a call whose wait expired, counters may be left
+// mid-count; this puts the scratch back in order without allocating.
+int fd_linear_noalloc_reset(void* stream) {
+  void* scratch = nullptr;
+  const int r = noalloc_scratch(&scratch);
+  if (r != FD_OK) return r;
+  const size_t bytes = streamk_ws_bytes() - counters_offset();  // counters, then the status word
+  return from_cuda(cudaMemsetAsync(static_cast<char*>(scratch) + counters_offset(), 0, bytes,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

@@ -16,10 +16,13 @@ import torch
 
 from fused_decode_b200 import _capi
 
-# Geometry of the stream-K GEMV (fd_gemv.cu): weight rows per block, columns
-# per step, warps per CTA, register pipeline depth.
+# Default geometry of the stream-K GEMV (csrc/fd_stream.cuh): weight rows per
+# block, columns per pipeline step (two 64-column TMA boxes), consumer warps
+# per CTA, shared-memory ring stages.  The library may shed ring stages when a
+# batch's activation rows need the shared memory; FD_GEMV_GEOMETRY overrides
+# producers, boxes and stages for tuning.
 GEMV_BLOCK_ROWS = 128
-GEMV_K_STEP = 32
+GEMV_K_STEP = 128
 GEMV_WARPS = 8
 GEMV_STAGES = 4
 GEMV_MAX_M = 16
@@ -201,7 +204,7 @@ def resolve_kind(kind: str | None) -> str:
 
 
 def linear_config(kind: str, n: int, k: int) -> tuple[int, int, int, int]:
-    """Tile geometry of the GEMV for this shape: (block rows, k step, warps, stages).
+    """Default tile geometry of the GEMV: (block rows, columns per step, consumer warps, ring stages).
 
     Replaces the reference's hand tile table (kernels.py:589-603).  The
     stream-K kernel balances any (N, K) over the SMs, so one geometry serves

@@ -125,13 +125,28 @@ int fd_linear_out(const void* x, int64_t sxm, int64_t sxk,
  *   - The first call on a device looks up that device's scratch address
  *     (set-up, done once per device; make it before any stream capture).
  *   - The scratch starts at zero when the library is loaded on a device, and
- *     every completed launch leaves its counters at zero again.
+ *     every completed launch leaves its counters at zero again; after a
+ *     launch whose wait expired, fd_linear_noalloc_reset() below restores it.
  *   - All calls on one device share the one scratch: calls that overlap in
  *     time (concurrent streams, threads) race; serialise them.
  *   - Returns FD_ERR_WORKSPACE when the device needs more scratch than the
  *     built-in size (fd_linear_workspace_bytes() above it, i.e. a GPU with more
  *     than 183 SMs); otherwise the return values of fd_linear_out. */
 size_t fd_linear_noalloc_scratch_bytes(void);
+/* Health of the scratch (no counterpart in the reference).  A call whose
+ * bounded in-kernel wait expired (a stalled copy engine, a pre-empted GPU)
+ * leaves invalid outputs, a non-zero status word and possibly half-counted
+ * split-K counters in the shared scratch -- which would make every later call
+ * on that device reduce the wrong blocks.  A caller without a workspace of
+ * its own cannot reach that memory, so:
+ *   fd_linear_noalloc_status: the status word after all work enqueued on
+ *     `stream` so far (0: no wait expired); waits for `stream` to finish.
+ *   fd_linear_noalloc_reset: zero the counters and the status word on
+ *     `stream` (asynchronous, allocates nothing); the next call then starts
+ *     from a clean scratch.
+ * Both use the scratch of the current device. */
+int fd_linear_noalloc_status(int32_t* status, void* stream);
+int fd_linear_noalloc_reset(void* stream);
 int fd_linear_out_noalloc(const void* x, int64_t sxm, int64_t sxk,
                           const void* w, int64_t swn, int64_t swk,
                           const void* bias, int32_t bias_dtype, int64_t sbias,

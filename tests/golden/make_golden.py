@@ -3,7 +3,7 @@
 Runs the reference package's own correctness formulation
 (``fused_decode.reference`` -- PyTorch on CPU) on seeded inputs and stores the
 inputs and outputs as ``golden.npz`` plus a ``manifest.json``.  The shapes
-follow the reference's tests (tests/test_ops.py:42-171) and the BASELINE
+follow the reference's tests (tests/test_ops.py:42-171) and the benchmark
 configurations, scaled down so the fixtures stay small.
 
 This script needs the reference's ``src`` directory (the folder holding the
@@ -96,7 +96,7 @@ def main() -> None:
         wt = torch.randn(32, dtype=torch.float32)
         w.add("rms_norm", dname, {"eps": 1e-6, "layout": "transposed"}, {"x": x, "weight": wt},
               {"y": R.rms_norm_reference(x, wt)})
-        # BASELINE config 0 widths, 8 rows: w = 1 + 0.1 N(0,1), eps = 1e-5
+        # add+RMSNorm benchmark widths, 8 rows: w = 1 + 0.1 N(0,1), eps = 1e-5
         torch.manual_seed(0)
         x = torch.randn(8, 4096, dtype=dt)
         r = torch.randn(8, 4096, dtype=dt)
@@ -114,7 +114,7 @@ def main() -> None:
         y, ro = R.add_rms_norm_reference(x, r, wt)
         w.add("add_rms_norm", dname, {"eps": 1e-6}, {"x": x, "residual": r, "weight": wt},
               {"y": y, "residual_out": ro})
-        # swiglu (tests/test_ops.py:106-113) and the BASELINE width
+        # swiglu (tests/test_ops.py:106-113) and the benchmark width
         for seed, shape, scale in [(5, (3, 128), 1.0), (0, (2, 14336), 1.0), (11, (4, 512), 30.0)]:
             torch.manual_seed(seed)
             g = (torch.randn(*shape) * scale).to(dt)
@@ -131,7 +131,7 @@ def main() -> None:
         s = torch.randn(1, 8, 1, 64, dtype=torch.float32)
         w.add("rope", dname, {"layout": "transposed"}, {"x": x, "cos": c, "sin": s},
               {"y": R.rope_reference(x, c, s)})
-        # rope with theta = 500000 tables, 16 positions
+        # rope with theta = 500000 tables (the RoPE benchmark tables), 16 positions
         torch.manual_seed(0)
         x = torch.randn(1, 16, 32, 128, dtype=dt)
         c, s = theta_tables(16, 128, 500000.0, dt)
@@ -152,7 +152,7 @@ def main() -> None:
         row = torch.randn(4, 64, dtype=dt)
         w.add("linear", dname, {"layout": "transposed_weight"}, {"x": x, "weight": wt, "row_add": row},
               {"y": R.linear_reference(x, wt, row_add=row)})
-        # BASELINE config 2 distributions: W ~ N(0, 0.02), x ~ N(0, 1), fp32 bias / row_add
+        # GEMV sweep distributions: W ~ N(0, 0.02), x ~ N(0, 1), fp32 bias / row_add
         for m in (1, 2, 4, 8, 16):
             torch.manual_seed(100 + m)
             x = torch.randn(m, 2048, dtype=dt)
@@ -161,7 +161,7 @@ def main() -> None:
             row = torch.randn(m, 40, dtype=torch.float32)
             w.add("linear", dname, {}, {"x": x, "weight": wt, "bias": b, "row_add": row},
                   {"y": R.linear_reference(x, wt, b, row_add=row)})
-        # post_attn_mlp (tests/test_ops.py:159-171) and BASELINE config 3 distributions
+        # post_attn_mlp (tests/test_ops.py:159-171) and Llama-3-8B MLP benchmark distributions
         torch.manual_seed(9)
         hid, inner = 64, 128
         x = torch.randn(4, hid, dtype=dt)

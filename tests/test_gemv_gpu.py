@@ -1,7 +1,7 @@
-"""GEMV family and fused MLP at the BASELINE shapes, plus edge cases.
+"""GEMV family and fused MLP at the benchmark shapes, plus edge cases.
 
 Comparator: the CPU oracle (fp32 numpy restatement of reference.py:50-79).
-Tolerance: BASELINE's atol = rtol = 1e-2 for fp16/bf16 outputs against the
+Tolerance: the parity bar atol = rtol = 1e-2 for fp16/bf16 outputs against the
 fp32 reference.  Split-K partial sums are reduced in a fixed order, so the
 CUDA results are also checked to be bit-reproducible run to run.
 """
@@ -37,7 +37,7 @@ def _gen(seed):
     return g
 
 
-# M in {1,2,4,8,16} x (N,K) in the Llama-3-8B shapes.
+# The GEMV sweep: M in {1,2,4,8,16} x (N,K) in the Llama-3-8B shapes.
 SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (28672, 4096)]
 
 
@@ -127,7 +127,7 @@ def _mlp_weights(h, i, dtype, seed):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("m", [1, 3, 8, 16])
 def test_post_attn_mlp_llama8b(dtype, m):
-    """hidden [M, 4096], w_gate_up [28672, 4096], w_down [4096, 14336]."""
+    """Llama-3-8B widths: hidden [M, 4096], w_gate_up [28672, 4096], w_down [4096, 14336]."""
     h, i = 4096, 14336
     nw, wgu, wd = _mlp_weights(h, i, dtype, 11)
     x = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(12 + m))

@@ -8,7 +8,7 @@ cut the weights, that the per-rank fp32 partials summed by one
 gloo ranks agrees on the result.  Tolerance: the fp32 partials are summed in a
 different order than the unsharded dot products, so the result may differ from
 the unsharded oracle by one rounding step of the activation dtype; checked as
-at most 1 ulp and within BASELINE's atol = rtol = 1e-2.
+at most 1 ulp and within the parity bar atol = rtol = 1e-2.
 """
 
 import datetime

@@ -5,7 +5,7 @@
   are summed in rank order and finished by ``residual_add_out`` -- the TP layer
   without the collective.  Compared with the oracle's partials summed the same
   way (within one bf16 rounding step: rtol 2^-7, atol 1e-3), and with the
-  unsharded oracle layer within BASELINE's atol = rtol = 1e-2.
+  unsharded oracle layer within the parity bar atol = rtol = 1e-2.
 * Two or more GPUs: ranks over NCCL run chained TP layers end to end
   (``TPPostAttnMlp.__call__``, one ``all_reduce`` per layer); skipped when the
   machine has fewer than two GPUs.
@@ -129,7 +129,7 @@ def _rope_tables(positions, dim, theta=500000.0):
 
 @pytest.mark.parametrize("m", [1, 4, 8])
 def test_tp_decode_block_llama70b(m):
-    """BASELINE config 5 at full Llama-3-70B widths (hidden 8192, intermediate
+    """The tensor-parallel decode block at full Llama-3-70B widths (hidden 8192, intermediate
     28672, 64 query / 8 KV heads of 128): add_rms_norm, RoPE on q and k, then
     the MLP with gate/up column-sharded and down row-sharded over 8 emulated
     ranks on one GPU (the allreduce is the fp32 sum of the rank partials), then
