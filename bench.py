@@ -828,6 +828,14 @@ def run_ours(args) -> None:
     e2e_s = wall(e2e_graph_step, args.steps)
     e2e_eager_s = wall(e2e_eager_step, max(3, args.steps // 10))
 
+    # ---- the tensor-parallel decode block at Llama-3-70B widths (every N)
+    block = None
+    if not args.no_block:
+        del graph_gu, graph_dn
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        block = run_tp_block(torch, device, world, rank, args, pk, barrier, max_over_ranks)
+
     # ---- CPU baseline (rank 0, N=1 only): the reference's PyTorch-eager CPU path, bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -877,6 +885,8 @@ def run_ours(args) -> None:
                 "two_kernel_us_per_layer": two_kernel_us,
             },
             "ops": ops,
+            "ops_parity_ok": (all(r.get("parity_ok", True) for r in ops.values()) if ops else None),
+            "tp_block_70b": block,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_s * 1e6 / LAYERS, "unit": "us/layer",
                     "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
@@ -891,7 +901,7 @@ def run_ours(args) -> None:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        del stack1, stack8, graph_gu, graph_dn
+        del stack1, stack8
         torch.cuda.synchronize()
         if exchange is not None:
             exchange.close()
@@ -971,6 +981,7 @@ def main() -> None:
     ap.add_argument("--cpu-evals", type=int, default=20, help="timed CPU-baseline layer evaluations")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="skip the standalone-op measurements")
+    ap.add_argument("--no-block", action="store_true", help="skip the Llama-3-70B tensor-parallel decode block")
     ap.add_argument("--tp-collective", choices=("nvlink", "nccl"), default="nvlink",
                     help="N>1: partial sums over the NVLink exchange buffers (default) or NCCL all_reduce")
     ap.add_argument("--ncu-case", choices=NCU_CASES, default=None,
