@@ -127,6 +127,7 @@ SIGNATURES: dict[str, tuple] = {
             c_vp, c_size, c_vp,          # workspace, bytes, stream
         ],
     ),
+    "fd_post_attn_mlp_stack_launches": (c_i32, [c_i32, c_i32, c_i32, c_i64, c_i64, c_i32]),
     "fd_post_attn_mlp_stack_out": (
         c_i32,
         [

@@ -96,6 +96,32 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return OUT
 
 
+# The persistent stack kernel moves registers between its warpgroups with
+# setmaxnreg; its split (csrc/fd_stack.cu) fits a launch allotment of at
+# least this many registers per thread.  setmaxnreg.inc would wait forever
+# for registers the launch never had, so a build whose allotment is smaller
+# must not ship.
+STACK_MIN_LAUNCH_REGS = 160
+
+
+def _check_stack_registers(ptxas_log: str) -> None:
+    entry = None
+    seen = 0
+    for line in ptxas_log.splitlines():
+        if "Compiling entry function" in line:
+            entry = line
+        elif entry and "Used" in line and "registers" in line:
+            if "mlp_stack_kernel" in entry:
+                regs = int(line.split("Used")[1].split("registers")[0])
+                if regs < STACK_MIN_LAUNCH_REGS:
+                    raise RuntimeError(f"mlp_stack_kernel launches with {regs} registers per thread, below the "
+                                       f"{STACK_MIN_LAUNCH_REGS} its setmaxnreg split needs: {entry}")
+                seen += 1
+            entry = None
+    if seen == 0:
+        raise RuntimeError("no ptxas register report for mlp_stack_kernel")
+
+
 def _build_library(force: bool, verbose: bool) -> str:
     if not force and up_to_date():
         return OUT
@@ -106,7 +132,8 @@ def _build_library(force: bool, verbose: bool) -> str:
     for src in _sources():
         obj = os.path.join(BUILD_DIR, os.path.basename(src).replace(".cu", ".o"))
         objs.append(obj)
-        cmds.append([nvcc, *ARCH, *FLAGS, "-c", src, "-o", obj])
+        extra = ["-Xptxas", "-v"] if src.endswith("fd_stack.cu") else []
+        cmds.append([nvcc, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj])
 
     def run(cmd):
         if verbose:
@@ -117,9 +144,11 @@ def _build_library(force: bool, verbose: bool) -> str:
         return res.stderr
 
     with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, len(cmds))) as pool:
-        for err in pool.map(run, cmds):
+        for cmd, err in zip(cmds, pool.map(run, cmds)):
             if verbose and err:
                 print(err, file=sys.stderr)
+            if cmd[-3].endswith("fd_stack.cu"):
+                _check_stack_registers(err)
     tmp = OUT + ".tmp"
     run([nvcc, *ARCH, "-shared", "-o", tmp, *objs])
     os.replace(tmp, OUT)

@@ -36,7 +36,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
   const int64_t G = gridDim.x, c = blockIdx.x;
   const int64_t s0 = range_start(c, a.total, G);
   const int64_t s1 = range_start(c + 1, a.total, G);
-  const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided};
+  const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided, 0u, 1};
   unsigned char* nw_smem = r.xreg + gateup_x_bytes(a.m, a.ks, a.boxes);  // GATEUP: norm weight copy
 
   if (threadIdx.x == 0) {
@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
   }
   // consumer warps
   grid_dep_wait();
-  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, r, s_sumsq, nw_smem, &s_nw_bar);
+  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, a.hidden, r, s_sumsq, nw_smem, &s_nw_bar);
   grid_dep_launch();
   consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort, ms);
 }
@@ -422,6 +422,11 @@ int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers, const void* c
   // mid hold the inner activations; `out` receives only the last layer.
   char* ping[2] = {ws.tail + align256(static_cast<size_t>(m) * i * 2),
                    ws.tail + align256(static_cast<size_t>(m) * i * 2) + align256(static_cast<size_t>(m) * h * 2)};
+  // One persistent kernel for the whole stack where it applies (bit-identical
+  // to the chain below); otherwise two launches per layer.
+  const int rp = mlp_stack_persistent(hidden, layers, norm_w, norm_dtype, w_gate_up, s_gu, w_down, s_down, out,
+                                      dtype, m, h, i, eps, kind, ws, ws.tail, ping[0], ping[1], st);
+  if (rp != FD_ERR_UNSUPPORTED) return rp;
   const void* cur = hidden;
   for (int l = 0; l < layers; ++l) {
     void* dst = l == layers - 1 ? out : ping[l & 1];

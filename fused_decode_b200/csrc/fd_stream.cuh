@@ -60,7 +60,12 @@ constexpr uint64_t kWaitNs = 2000000000ull;      // bounded mbarrier waits: 2 s
 constexpr int kStatusFullTimeout = 1;
 constexpr int kStatusEmptyTimeout = 2;
 
-enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1 };
+// LINEAR: a GEMV whose activation boxes arrive by TMA with the weight boxes.
+// GATEUP: the MLP gate/up stage; the normalised batch is held in shared memory.
+// LINEAR_X: a GEMV whose activation columns for the CTA's step range were
+// staged in shared memory by the consumers (the persistent MLP stack's down
+// projection: its activation is written inside the same kernel).
+enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2 };
 
 // One phase of streaming: a GEMV (LINEAR) or the MLP gate/up stage (GATEUP).
 struct GemvArgs {
@@ -314,6 +319,45 @@ struct Epilogue<T, NT, MODE_LINEAR> {
   }
 };
 
+// The persistent MLP stack's per-layer pointers: its consumers set them at
+// the start of each phase (one shared copy per CTA), so the phase's GemvArgs
+// stay in kernel parameter space -- read as constant operands, holding no
+// registers in the streaming loop -- while the layer changes.
+__shared__ const void* sx_ra;  // LINEAR_X: the residual rows added in the epilogue
+__shared__ char* sx_y;         // LINEAR_X: the output rows
+
+// LINEAR_X: y = round(acc + row_add), with row_add and y from sx_ra / sx_y
+// (the stack's down projection: no bias, 16-bit output).
+template <typename T, int NT>
+struct Epilogue<T, NT, MODE_LINEAR_X> {
+  FD_DEV static void extras(const GemvArgs& a, int64_t blk, Acc<NT>& ex) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const void* ra = sx_ra;
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
+        const int col = 8 * t + 2 * q + (e & 1);
+        ex.v[t][e] = (row < a.n && col < a.m) ? load_as_f32_cg(ra, a.ra_dtype, col * a.srm + row * a.srn) : 0.f;
+      }
+  }
+  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& ex, float* /*xchg*/) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    T* y = reinterpret_cast<T*>(sx_y);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
+        const int col = 8 * t + 2 * q + (e & 1);
+        if (row < a.n && col < a.m) y[col * a.sym + row * a.syn] = from_f32<T>(acc.v[t][e] + ex.v[t][e]);
+      }
+  }
+};
+
 // Gate/up + SwiGLU: warps 0..3 hold gate rows, warps 4..7 the matching up rows.
 // gate and up are rounded to T first, as the reference rounds gate_up
 // (reference.py:390, ops.py:313), then mid = round(silu(gate) * up).
@@ -452,18 +496,25 @@ FD_DEV void settle(const GemvArgs& a, int64_t blk, float* xchg, int64_t G, int* 
 // counter), so the consumer warps go on streaming instead of waiting through
 // those memory round trips; if the announcer finds this CTA completed the
 // block, the consumers reduce it at the end of their range.
+// One kernel may run several phases: `parity` is the phase of the two
+// mbarriers for this phase's hand-off (they complete once per phase that has
+// a mid block), and the flags carry `tag` (unique per phase, never 0) rather
+// than 1, so no flag needs resetting between phases.
 struct MidSync {
   uint64_t* ready;  // consumer warps -> announcer: slot 0 written (count GW)
   uint64_t* done;   // announcer -> consumers: published, *last valid (count 1)
   int* last;
   int* fast;        // announcer -> consumers: every other contributor of the final block has published
   int* decided;     // consumers -> announcer: the final block's path is chosen, stop watching
+  uint32_t parity;
+  int tag;
 };
 
 // This CTA holds the first step of its final block but not the whole block:
 // the other contributors (later CTAs) process their parts at the start of
 // their ranges, so they have usually published before this CTA gets there.
 FD_DEV bool head_of_final(int64_t s0, int64_t s1, int64_t ks) {
+  if (s1 <= s0) return false;  // an empty range (a CTA past a phase's grid) has no final block
   const int64_t bf = (s1 - 1) / ks;
   return s0 <= bf * ks && s1 < (bf + 1) * ks;
 }
@@ -476,9 +527,9 @@ FD_DEV void watch_final(const GemvArgs& a, const MidSync& ms, int64_t s0, int64_
   const int64_t bf = (s1 - 1) / a.ks;
   const int others = static_cast<int>(cta_of((bf + 1) * a.ks - 1, a.total, G) - c);
   const uint64_t t0 = globaltimer();
-  while (!*reinterpret_cast<volatile int*>(ms.decided)) {
+  while (*reinterpret_cast<volatile int*>(ms.decided) != ms.tag) {
     if (ld_acquire_gpu(a.counters + bf) == others) {
-      *reinterpret_cast<volatile int*>(ms.fast) = 1;
+      *reinterpret_cast<volatile int*>(ms.fast) = ms.tag;
       return;
     }
     if (globaltimer() - t0 > kWaitNs) return;
@@ -493,7 +544,7 @@ FD_DEV void announce_mid(const GemvArgs& a, const MidSync& ms, int64_t s0, int64
   if (!has_mid_block(s0, s1, a.ks)) return;
   const int64_t b0 = s0 / a.ks;
   int last = 0;
-  if (mbar_wait(ms.ready, 0)) {
+  if (mbar_wait(ms.ready, ms.parity)) {
     if (!*reinterpret_cast<volatile int*>(s_abort)) {
       __threadfence();  // the consumers' slot stores (ordered before the mbarrier) first
       const int64_t cf = cta_of(b0 * a.ks, a.total, G);
@@ -656,12 +707,14 @@ FD_DEV void load8_smem_as_f32(const unsigned char* p, int dtype, float* f) {
 // REGS: 16-byte vectors of hidden held per thread per group of rows.
 // NR: the exact row count when it is known at compile time (0: m at run time).
 template <typename T, int JV, int REGS = 8, int NR = 0>
-FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
-                      uint64_t* nw_bar);
+FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
+                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity);
 
+// `hidden`: the rows to normalise (a.hidden for a single launch; the stack
+// passes each layer's input).
 template <typename T>
-FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
-                         uint64_t* nw_bar) {
+FD_DEV void norm_to_smem(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
+                         const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity = 0) {
   const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
   const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;
   // The prologue runs right after the launch, so its unrolled code is on the
@@ -671,33 +724,33 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_M
   // Other batches that fit four vectors per thread take the 4-vector group;
   // wider ones keep 8 vectors, so fewer groups (fewer load round trips).
   if (jv == 2 && a.m == 1) {
-    norm_rows<T, 2, 2, 1>(a, r, s_sumsq, nw, nw_bar);
+    norm_rows<T, 2, 2, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   if (jv == 2 && a.m == 2) {
-    norm_rows<T, 2, 4, 2>(a, r, s_sumsq, nw, nw_bar);
+    norm_rows<T, 2, 4, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   if (jv == 1 && a.m == 1) {
-    norm_rows<T, 1, 1, 1>(a, r, s_sumsq, nw, nw_bar);
+    norm_rows<T, 1, 1, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   if (jv == 1 && a.m <= 4) {
-    norm_rows<T, 1, 4>(a, r, s_sumsq, nw, nw_bar);
+    norm_rows<T, 1, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   switch (jv) {
-    case 1: norm_rows<T, 1>(a, r, s_sumsq, nw, nw_bar); break;
-    case 2: norm_rows<T, 2>(a, r, s_sumsq, nw, nw_bar); break;
-    case 3: norm_rows<T, 3>(a, r, s_sumsq, nw, nw_bar); break;
-    case 4: norm_rows<T, 4>(a, r, s_sumsq, nw, nw_bar); break;
-    default: norm_rows<T, 0>(a, r, s_sumsq, nw, nw_bar); break;
+    case 1: norm_rows<T, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    case 2: norm_rows<T, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    case 3: norm_rows<T, 3>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    case 4: norm_rows<T, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    default: norm_rows<T, 0>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
   }
 }
 
 template <typename T, int JV, int REGS, int NR>
-FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX], const unsigned char* nw,
-                      uint64_t* nw_bar) {
+FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
+                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned char* xs = r.xreg;
   const int nvec = static_cast<int>(a.k / 8);
@@ -716,7 +769,7 @@ FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]
         const int v = tid + j * CONSUMERS;
         hv[e] = make_uint4(0, 0, 0, 0);
         if (rr < nr && v < nvec)
-          hv[e] = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) +
+          hv[e] = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(hidden) +
                                                          (r0 + rr) * a.hidden_stride) + v);
       }
       float ss[REGS];
@@ -742,7 +795,7 @@ FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]
         }
       }
       consumer_sync();
-      if (r0 == 0 && !mbar_wait(nw_bar, 0)) atomicOr(a.status, kStatusFullTimeout);
+      if (r0 == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
       // one scale per row of the group, then a short loop over the vectors
       float inv[rows_per_group];
 #pragma unroll
@@ -776,7 +829,7 @@ FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]
   } else {
   // Very wide rows: two passes per row, loads of a pass in flight together.
   for (int mrow = 0; mrow < a.m; ++mrow) {
-    const uint4* hr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.hidden) + mrow * a.hidden_stride);
+    const uint4* hr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(hidden) + mrow * a.hidden_stride);
     float ss = 0.f;
     for (int v = tid; v < nvec; v += CONSUMERS) {
       float f[8];
@@ -791,7 +844,7 @@ FD_DEV void norm_rows(const GemvArgs& a, const Ring& r, float (*s_sumsq)[MT_MAX]
 #pragma unroll
     for (int w = 0; w < GW; ++w) tot += s_sumsq[w][0];
     const float inv = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
-    if (mrow == 0 && !mbar_wait(nw_bar, 0)) atomicOr(a.status, kStatusFullTimeout);
+    if (mrow == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
     for (int v = tid; v < nvec_pad; v += CONSUMERS) {
       uint4 packed = make_uint4(0, 0, 0, 0);
       if (v < nvec) {
@@ -849,7 +902,9 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
     }
     // activation box j of this step: [m rows x 128 B] (swizzled by row & 7)
     auto xbox = [&](int j) -> const unsigned char* {
-      return MODE == MODE_LINEAR ? r.xreg + (s * B + j) * r.x_slot : r.xreg + ((ck * B + j) * a.m) * 128;
+      if (MODE == MODE_LINEAR) return r.xreg + (s * B + j) * r.x_slot;
+      if (MODE == MODE_LINEAR_X) return r.xreg + ((it * B + j) * a.m) * 128;
+      return r.xreg + ((ck * B + j) * a.m) * 128;
     };
     if (KIND == 0) {
       uint4 xa[MAX_BOXES][NT][2];
@@ -953,8 +1008,8 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
         Acc<NT> ex;
         Epilogue<T, NT, MODE>::extras(a, cb, ex);
         if (threadIdx.x == 0) {
-          *s_last = *reinterpret_cast<volatile int*>(ms.fast);
-          *reinterpret_cast<volatile int*>(ms.decided) = 1;
+          *s_last = *reinterpret_cast<volatile int*>(ms.fast) == ms.tag;
+          *reinterpret_cast<volatile int*>(ms.decided) = ms.tag;
         }
         consumer_sync();
         if (*s_last) {
@@ -980,7 +1035,7 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
     }
   }
   if (has_mid_block(s0, s1, a.ks)) {
-    if (!mbar_wait(ms.done, 0)) {
+    if (!mbar_wait(ms.done, ms.parity)) {
       atomicOr(a.status, kStatusFullTimeout);
       *s_abort = 1;
       return false;
@@ -1115,3 +1170,14 @@ Geometry choose_geometry(XBytes xbytes) {
 inline int from_cuda(cudaError_t e) { return e == cudaSuccess ? FD_OK : FD_ERR_LAUNCH; }
 
 }  // namespace fd_stream
+
+namespace fd_host {
+// A post_attn_mlp stack as one persistent kernel (fd_stack.cu).  mid, ping0
+// and ping1 are the workspace's intermediate buffers ([m, i], [m, h], [m, h]).
+// FD_ERR_UNSUPPORTED: not served by the persistent kernel (use the chain).
+int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* norm_w, int32_t norm_dtype,
+                         const void* const* w_gate_up, int64_t s_gu, const void* const* w_down, int64_t s_down,
+                         void* out, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
+                         const fd_stream::Workspace& ws, void* mid, void* ping0, void* ping1, cudaStream_t st);
+int mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i, int32_t kind);
+}  // namespace fd_host

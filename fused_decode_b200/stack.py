@@ -17,6 +17,7 @@ from typing import Sequence
 
 import torch
 
+from fused_decode_b200 import _capi
 from fused_decode_b200 import kernels as K
 from fused_decode_b200.ops import _check_activation, post_attn_mlp
 
@@ -81,8 +82,14 @@ class MlpStack:
 
     @property
     def launches_per_replay(self) -> int:
-        """Kernel launches of this library per replay."""
-        return 2 * len(self.layers)
+        """Kernel launches of this library per replay: one persistent kernel
+        per 32 layers where the stack entry point runs one, else two per layer."""
+        if not self.fused:
+            return 2 * len(self.layers)
+        nw0, wgu0, wd0 = self.layers[0]
+        return int(_capi.load().fd_post_attn_mlp_stack_launches(
+            len(self.layers), _capi.dtype_code(nw0.dtype), int(self.static_in.shape[0]), self.h,
+            int(wd0.shape[1]), _capi.FD_KIND_DOT if self.kind == "dot" else _capi.FD_KIND_SIMT))
 
     def replay(self) -> torch.Tensor:
         self.graph.replay()

@@ -98,7 +98,7 @@ size_t fd_linear_workspace_bytes(int32_t m, int64_t n, int64_t k);
 /* Byte offset, inside any workspace above, of a 32-bit status word the
  * kernels OR error bits into (1: a consumer's shared-memory pipeline wait
  * expired, 2: a producer's wait expired, 8: a tensor-parallel exchange wait
- * expired).  Zero means no error.  After a non-zero
+ * expired, 16: a grid-wide barrier wait of the persistent MLP stack expired).  Zero means no error.  After a non-zero
  * status the outputs of that launch are invalid and the workspace must be
  * zero-filled again before reuse. */
 size_t fd_workspace_status_offset(void);
@@ -182,11 +182,20 @@ int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dt
 
 /* `layers` consecutive post_attn_mlp layers (layer l reads layer l-1's
  * output): norm_w, w_gate_up and w_down are HOST arrays of `layers` device
- * pointers with shared shapes, strides and dtypes.  Two launches per layer,
- * enqueued by one call; intermediate activations live in the workspace and
- * only the last layer's output is written to `out`.  The workspace is
- * fd_post_attn_mlp_workspace_bytes(m, h, i).
+ * pointers with shared shapes, strides and dtypes.  Intermediate activations
+ * live in the workspace and only the last layer's output is written to
+ * `out`.  The workspace is fd_post_attn_mlp_workspace_bytes(m, h, i).
+ * kind = FD_KIND_DOT runs the stack as ONE persistent cooperative kernel per
+ * 32 layers (one CTA per SM; the weight stream runs on across layer and
+ * phase boundaries while grid-wide barriers order the activations; status
+ * bit 16: a barrier wait expired); otherwise, or where the batch does not
+ * fit its shared-memory plan, two launches per layer.  Both give the same
+ * bits as one fd_post_attn_mlp_out call per layer.
  * Replaces a loop of post_attn_mlp calls (reference ops.py:283-315). */
+/* Kernel launches one fd_post_attn_mlp_stack_out call of this shape makes
+ * (no counterpart in the reference). */
+int fd_post_attn_mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,
+                                    int32_t kind);
 int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers,
                                const void* const* norm_w, int32_t norm_dtype,
                                const void* const* w_gate_up, int64_t s_gu,

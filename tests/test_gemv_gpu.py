@@ -16,6 +16,7 @@ pytestmark = pytest.mark.gpu
 
 from fused_decode_b200 import linear_decode, post_attn_mlp  # noqa: E402
 from fused_decode_b200 import kernels as K  # noqa: E402
+from fused_decode_b200 import _capi  # noqa: E402
 
 TOL = {"rtol": 1e-2, "atol": 1e-2}
 _NAME = {torch.float16: "float16", torch.bfloat16: "bfloat16"}
@@ -232,7 +233,7 @@ def test_post_attn_mlp_stack_fused(m):
         ref = O.post_attn_mlp(ref, _np(nw), _np(wgu), _np(wd), 1e-5, "bfloat16")
     _close(fused_out, ref, {"rtol": 2e-2, "atol": 2e-2})
     stack = MlpStack(ws, m, 1e-5, kind="dot")
-    assert stack.fused and stack.launches_per_replay == 2 * layers
+    assert stack.fused and stack.launches_per_replay == 1  # one persistent kernel
     for _ in range(2):
         torch.testing.assert_close(stack(x0), fused_out, rtol=0, atol=0)
 
@@ -291,3 +292,50 @@ def test_post_attn_mlp_stack_simt_and_fp32_norm():
 def test_zz_no_pipeline_timeouts_after_stacks():
     torch.cuda.synchronize()
     assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_persistent_stack_llama8b(m):
+    """The persistent one-kernel stack at Llama-3-8B widths (4 layers): the
+    same bits as one post_attn_mlp call per layer (two launches each), each of
+    which matches the oracle on its own input at atol = rtol = 1e-2; captured
+    in a CUDA graph it replays the same bits."""
+    from fused_decode_b200.stack import MlpStack
+
+    h, i, layers = 4096, 14336, 4
+    dtype = torch.bfloat16
+    ws = [_mlp_weights(h, i, dtype, 600 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(60 + m))
+    out = torch.empty_like(x0)
+    K.post_attn_mlp_stack_out(x0, ws, out, 1e-5, "dot")
+    x = x0
+    for nw, wgu, wd in ws:
+        y = post_attn_mlp(x, nw, wgu, wd, 1e-5, kind="dot")
+        # each layer against the oracle given that layer's own input
+        _close(y, O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-5, "bfloat16"))
+        x = y
+    assert torch.equal(out, x)
+    stack = MlpStack(ws, m, 1e-5, kind="dot")
+    assert stack.launches_per_replay == 1
+    for _ in range(3):
+        assert torch.equal(stack(x0), out)
+    torch.cuda.synchronize()
+    assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+
+
+def test_persistent_stack_two_launches():
+    """33 layers take two persistent launches (32 + 1): the hand-over between
+    them, and the barrier counter left at zero by the first, give the chain's bits."""
+    h, i, layers, m = 256, 512, 33, 2
+    dtype = torch.bfloat16
+    ws = [_mlp_weights(h, i, dtype, 700 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(70))
+    lib = _capi.load()
+    assert lib.fd_post_attn_mlp_stack_launches(layers, _capi.dtype_code(dtype), m, h, i, _capi.FD_KIND_DOT) == 2
+    for _ in range(2):
+        out = torch.empty_like(x0)
+        K.post_attn_mlp_stack_out(x0, ws, out, 1e-6, "dot")
+        x = x0
+        for nw, wgu, wd in ws:
+            x = post_attn_mlp(x, nw, wgu, wd, kind="dot")
+        assert torch.equal(out, x)
