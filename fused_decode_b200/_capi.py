@@ -128,6 +128,18 @@ SIGNATURES: dict[str, tuple] = {
         ],
     ),
     "fd_post_attn_mlp_stack_launches": (c_i32, [c_i32, c_i32, c_i32, c_i64, c_i64, c_i32]),
+    "fd_post_attn_mlp_tp_stack_out": (
+        c_i32,
+        [
+            c_vp, c_i32,                 # hidden, layers
+            c_vp, c_i32,                 # norm_w (host array), norm_dtype
+            c_vp, c_i64, c_vp, c_i64,    # w_gate_up (host array), s_gu, w_down (host array), s_down
+            c_vp, c_i32, c_i32, c_i64, c_i64,  # out, dtype, m, h, i
+            c_f32, c_i32, c_i32, c_i32,  # eps, kind, rank, world
+            c_vp, c_i32,                 # exchange (void* const*), m_max
+            c_vp, c_size, c_vp,          # workspace, bytes, stream
+        ],
+    ),
     "fd_post_attn_mlp_stack_out": (
         c_i32,
         [

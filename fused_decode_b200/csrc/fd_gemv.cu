@@ -402,6 +402,46 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
   return tp_reduce_launch(static_cast<char*>(exchange[rank]), world, m, m_max, h, hidden, out, dtype, ws.status, st);
 }
 
+int fd_post_attn_mlp_tp_stack_out(const void* hidden, int32_t layers, const void* const* norm_w, int32_t norm_dtype,
+                                  const void* const* w_gate_up, int64_t s_gu, const void* const* w_down,
+                                  int64_t s_down, void* out, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps,
+                                  int32_t kind, int32_t rank, int32_t world, void* const* exchange, int32_t m_max,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace fd_host;
+  if (layers < 0 || !norm_w || !w_gate_up || !w_down) return FD_ERR_ARG;
+  if (world < 1 || world > kMaxTpWorld || rank < 0 || rank >= world || !exchange) return FD_ERR_ARG;
+  if (m_max < 1 || m_max > MT_MAX || m > m_max) return FD_ERR_ARG;
+  for (int k = 0; k < world; ++k)
+    if (!exchange[k]) return FD_ERR_ARG;
+  if (layers == 0) return check_mlp_args(hidden, hidden, norm_dtype, hidden, s_gu, dtype, m, h, i, kind);
+  for (int l = 0; l < layers; ++l) {
+    int r = check_mlp_args(hidden, norm_w[l], norm_dtype, w_gate_up[l], s_gu, dtype, m, h, i, kind);
+    if (r == FD_OK) r = check_down(w_down[l], s_down, out, dtype, dtype, i);
+    if (r != FD_OK) return r;
+  }
+  if (m == 0 || h == 0) return FD_OK;
+  if (!workspace || workspace_bytes < fd_post_attn_mlp_workspace_bytes(m, h, i)) return FD_ERR_WORKSPACE;
+  const Workspace ws = carve(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ping[2] = {ws.tail + align256(static_cast<size_t>(m) * i * 2),
+                   ws.tail + align256(static_cast<size_t>(m) * i * 2) + align256(static_cast<size_t>(m) * h * 2)};
+  const int rp = mlp_stack_persistent(hidden, layers, norm_w, norm_dtype, w_gate_up, s_gu, w_down, s_down, out,
+                                      dtype, m, h, i, eps, kind, ws, ws.tail, ping[0], ping[1], st, rank, world,
+                                      exchange, m_max);
+  if (rp != FD_ERR_UNSUPPORTED) return rp;
+  // three launches per layer (fd_post_attn_mlp_tp_out)
+  const void* cur = hidden;
+  for (int l = 0; l < layers; ++l) {
+    void* dst = l == layers - 1 ? out : ping[l & 1];
+    const int r = fd_post_attn_mlp_tp_out(cur, norm_w[l], norm_dtype, w_gate_up[l], s_gu, w_down[l], s_down, dst,
+                                          dtype, m, h, i, eps, kind, rank, world, exchange, m_max, workspace,
+                                          workspace_bytes, stream);
+    if (r != FD_OK) return r;
+    cur = dst;
+  }
+  return FD_OK;
+}
+
 int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers, const void* const* norm_w, int32_t norm_dtype,
                                const void* const* w_gate_up, int64_t s_gu, const void* const* w_down,
                                int64_t s_down, void* out, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps,

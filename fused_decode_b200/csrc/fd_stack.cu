@@ -55,6 +55,7 @@ constexpr int kConsumerRegs = 208;
 constexpr int kHelperRegs = 56;
 static_assert(8 * 32 * kConsumerRegs + 4 * 32 * kHelperRegs <= kStackThreads * 160, "register split");
 constexpr int kStatusBarrierTimeout = 16;
+constexpr int kStatusTpTimeout = 8;  // as the tensor-parallel reduce kernel
 constexpr size_t kBarOffset = 128;  // barrier counter: inside the status area, its own 128-byte line
 constexpr int kDepartOffset = 16;   // departure counter: 16 ints after the barrier counter
 
@@ -69,12 +70,19 @@ struct StackParams {
   char* ping[2];
   const void* mid;
   int* bar;
+  char* tp_buf;     // tensor parallel: this rank's exchange buffer (its header holds the round number)
   int layers;       // layers of this launch
   int first_layer;  // index of its first layer in the whole stack
   int total_layers;
   int xact_bytes;   // activation part of the X region; the norm weight follows it
   int x_bytes;
 };
+
+FD_DEV uint2 ld_tagged_sys(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
 
 FD_DEV bool phase_wait(const int* bar, int target, int* status, int* s_abort) {
   if (ld_acquire_gpu(bar) >= target) return true;
@@ -110,41 +118,89 @@ FD_DEV void phase_arrive(int* bar) {
 // steps [s0, s1) of a LINEAR_X phase read, into the X region as chunks of
 // [m x 128 B] in step order, swizzled like a TMA tile (the layout the
 // consumers read).  Columns past k are zero.  Loads go through L2 (another
-// CTA wrote them in this kernel); four per thread are in flight at a time.
+// CTA wrote them in this kernel).  Under full HBM load an L2 round trip
+// takes microseconds, so each thread issues all its loads (up to U) before
+// its first store: one round trip for m <= 8 at the Llama widths.
 template <typename T>
 FD_DEV void stage_x(const GemvArgs& a, const Ring& r, const T* src, int64_t s0, int64_t s1) {
   const int m = a.m, B = r.B;
-  const int64_t nvec = (s1 - s0) * B * m * 8;
-  constexpr int U = 4;
-  for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += CONSUMERS * U) {
+  const int nvec = static_cast<int>((s1 - s0) * B * m * 8);
+  constexpr int U = 16;
+  for (int v0 = threadIdx.x; v0 < nvec; v0 += CONSUMERS * U) {
     uint4 val[U];
-    int64_t dst[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t v = v0 + static_cast<int64_t>(u) * CONSUMERS;
+      const int v = v0 + u * CONSUMERS;
       val[u] = make_uint4(0, 0, 0, 0);
-      dst[u] = -1;
       if (v < nvec) {
-        const int cc = static_cast<int>(v & 7);
-        const int64_t rc = v >> 3;  // chunk * m + row
-        const int mrow = static_cast<int>(rc % m);
-        const int64_t q = rc / m;
-        const int64_t it = q / B;
-        const int j = static_cast<int>(q - it * B);
-        const int64_t kk = (s0 + it) % a.ks;
-        const int64_t col = (kk * B + j) * KC + cc * 8;
+        const int cc = v & 7, rc = v >> 3;  // rc = chunk * m + row
+        const int mrow = rc % m, q = rc / m;
+        const int it = q / B, j = q - it * B;
+        const int64_t col = (((s0 + it) % a.ks) * B + j) * KC + cc * 8;
         if (col < a.k) val[u] = __ldcg(reinterpret_cast<const uint4*>(src + mrow * a.k + col));
-        dst[u] = rc * 128 + ((cc ^ (mrow & 7)) << 4);
       }
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (dst[u] >= 0) st_shared16(r.xreg + dst[u], val[u]);
+    for (int u = 0; u < U; ++u) {
+      const int v = v0 + u * CONSUMERS;
+      if (v < nvec) {
+        const int cc = v & 7, rc = v >> 3, mrow = rc % m;
+        st_shared16(r.xreg + static_cast<int64_t>(rc) * 128 + ((cc ^ (mrow & 7)) << 4), val[u]);
+      }
+    }
   }
   consumer_sync();
 }
 
-template <typename T, int NT>
+// Tensor parallel: the reduce phase of one layer.  This CTA's share of the
+// m x h outputs: wait (bounded) until every rank's tagged partial word of
+// the round is in this rank's exchange buffer, sum the ranks in rank order
+// (the same bits on every rank), add the residual and round.  All consumer
+// threads.  False when a wait expired (status bit 8).
+template <typename T>
+FD_DEV bool tp_reduce_phase(const StackParams& p, int seq, const T* res, T* out, int* status) {
+  const int64_t n = p.da.n;
+  const int64_t total = static_cast<int64_t>(p.da.m) * n;
+  const int64_t G = gridDim.x, c = blockIdx.x;
+  const int64_t e1 = (c + 1) * total / G;
+  const int world = p.da.tp_world;
+  const int64_t rank_stride = static_cast<int64_t>(p.da.tp_mmax) * n;
+  const uint2* base = reinterpret_cast<const uint2*>(p.tp_buf + p.da.tp_data_off) + (seq & 1) * world * rank_stride;
+  bool ok = true;
+  for (int64_t e = c * total / G + threadIdx.x; e < e1 && ok; e += CONSUMERS) {
+    uint2 v[kMaxTpWorld];
+#pragma unroll
+    for (int rk = 0; rk < kMaxTpWorld; ++rk)
+      if (rk < world) v[rk] = ld_tagged_sys(base + rk * rank_stride + e);
+    const uint64_t t0 = globaltimer();
+#pragma unroll
+    for (int rk = 0; rk < kMaxTpWorld; ++rk) {
+      if (rk < world && ok) {
+        while (static_cast<int>(v[rk].y) != seq + 1) {
+          if (*reinterpret_cast<volatile int*>(status) != 0 || globaltimer() - t0 > kWaitNs) {
+            atomicOr(status, kStatusTpTimeout);
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+          v[rk] = ld_tagged_sys(base + rk * rank_stride + e);
+        }
+      }
+    }
+    if (ok) {
+      float sum = 0.f;
+#pragma unroll
+      for (int rk = 0; rk < kMaxTpWorld; ++rk)
+        if (rk < world) sum += __uint_as_float(v[rk].x);
+      out[e] = from_f32<T>(sum + to_f32(res[e]));
+    }
+  }
+  return ok;
+}
+
+// TP = false: phases gate/up, down (+ residual).  TP = true: gate/up, down
+// (partials published to every rank), reduce (+ residual).
+template <typename T, int NT, bool TP>
 __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __grid_constant__ StackParams p) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ int s_last, s_abort;
@@ -153,10 +209,12 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
   __shared__ __align__(8) uint64_t s_nw_full, s_nw_empty;
   __shared__ int s_mid_last, s_fast, s_decided;
   __shared__ const void* s_hidden;  // this layer's input rows (the gate/up phase's norm reads them)
+  __shared__ int s_seq0;            // tensor parallel: the exchange round of this launch's first layer
   // This CTA's step ranges and phase grids, kept in shared memory and read
   // where used, so they hold no registers across the streaming loops.
   __shared__ int64_t s_rng[6];
 
+  constexpr int PPL = TP ? 3 : 2;  // phases per layer
   const GemvArgs& ga = p.ga;
   const GemvArgs& da = p.da;
   const Ring r = carve_ring(smem_raw, ga.stages, ga.boxes, 0, p.x_bytes);
@@ -171,11 +229,12 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
   const int64_t Gg = G < ga.total ? G : ga.total, Gd = G < da.total ? G : da.total;
   const int64_t g0 = c < Gg ? range_start(c, ga.total, Gg) : 0, g1 = c < Gg ? range_start(c + 1, ga.total, Gg) : 0;
   const int64_t d0 = c < Gd ? range_start(c, da.total, Gd) : 0, d1 = c < Gd ? range_start(c + 1, da.total, Gd) : 0;
-  const int nphase = 2 * p.layers;
+  const int nphase = PPL * p.layers;
   const int gmid = has_mid_block(g0, g1, ga.ks) ? 1 : 0, dmid = has_mid_block(d0, d1, da.ks) ? 1 : 0;
   // mid-block hand-offs before phase ph: the parity of this phase's MidSync mbarriers
   auto mid_parity = [&](int ph) -> uint32_t {
-    return static_cast<uint32_t>((ph / 2) * (gmid + dmid) + ((ph & 1) ? gmid : 0)) & 1u;
+    const int k = ph % PPL;
+    return static_cast<uint32_t>((ph / PPL) * (gmid + dmid) + (k >= 1 ? gmid : 0) + (k >= 2 ? dmid : 0)) & 1u;
   };
   auto sync_for = [&](int ph) {
     return MidSync{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided, mid_parity(ph), ph + 1};
@@ -207,19 +266,24 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
     // the watch on the final block's counter
     grid_dep_wait();
     if (lane == 0) {
+      // the round number only changes at the very end of this kernel (below)
+      const int seq0 = TP ? *reinterpret_cast<volatile int*>(p.tp_buf) : 0;
       for (int ph = 0; ph < nphase; ++ph) {
-        const bool gu = (ph & 1) == 0;
-        const GemvArgs& a = gu ? ga : da;
+        const int k = ph % PPL;
         // the split-K counters of this phase are clean once the previous phase is done
         if (ph > 0 && !phase_wait(p.bar, static_cast<int>(G) * ph, status, &s_abort)) break;
-        const MidSync ms = sync_for(ph);
-        announce_mid(a, ms, gu ? g0 : d0, gu ? g1 : d1, gu ? Gg : Gd, &s_abort);
-        if (gu) watch_final(a, ms, g0, g1, Gg, c);
+        if (k < 2) {
+          const GemvArgs& a = k == 0 ? ga : da;
+          const MidSync ms = sync_for(ph);
+          announce_mid(a, ms, k == 0 ? g0 : d0, k == 0 ? g1 : d1, k == 0 ? Gg : Gd, &s_abort);
+          if (k == 0) watch_final(a, ms, g0, g1, Gg, c);
+        }
         if (*reinterpret_cast<volatile int*>(&s_abort)) break;
         if (ph == nphase - 1 && phase_wait(p.bar, static_cast<int>(G) * nphase, status, &s_abort)) {
           // every CTA has finished the launch's last phase and has no count left to wait for
           int* depart = p.bar + kDepartOffset;
           if (atomicAdd(depart, 1) == static_cast<int>(G) - 1) {
+            if (TP) *reinterpret_cast<volatile int*>(p.tp_buf) = seq0 + p.layers;  // rounds used by this launch
             *reinterpret_cast<volatile int*>(p.bar) = 0;
             *reinterpret_cast<volatile int*>(depart) = 0;
           }
@@ -264,10 +328,11 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
 
   // consumers
   grid_dep_wait();
+  if (TP && threadIdx.x == 0) s_seq0 = *reinterpret_cast<volatile int*>(p.tp_buf);
   const volatile int64_t* rng = s_rng;
   int64_t base = 0;
   for (int l = 0; l < p.layers; ++l) {
-    const int ph = 2 * l;
+    const int ph = PPL * l;
     const int gl = p.first_layer + l;
     // ---- gate/up of layer l
     if (ph > 0 && !consumer_phase_wait(p.bar, static_cast<int>(gridDim.x) * ph, status, &s_abort)) break;
@@ -281,11 +346,12 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
       break;
     base += rng[1] - rng[0];
     phase_arrive(p.bar);
-    // ---- down of layer l (+ hidden_l)
+    // ---- down of layer l: + hidden_l, or (tensor parallel) the partial to every rank
     if (!consumer_phase_wait(p.bar, static_cast<int>(gridDim.x) * (ph + 1), status, &s_abort)) break;
     if (threadIdx.x == 0) {
       sx_ra = gl == 0 ? p.hidden : p.ping[(gl - 1) & 1];
       sx_y = static_cast<char*>(gl == p.total_layers - 1 ? p.out : p.ping[gl & 1]);
+      if (TP) sx_seq = s_seq0 + l;
     }
     stage_x<T>(da, r, static_cast<const T*>(p.mid), rng[2], rng[3]);  // ends with a consumer barrier
     if (!consume_phase<T, NT, 0, 1, MODE_LINEAR_X>(da, r, rng[2], rng[3], base, rng[5], blockIdx.x, &s_last,
@@ -293,6 +359,15 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
       break;
     base += rng[3] - rng[2];
     phase_arrive(p.bar);
+    if (TP) {
+      // ---- reduce of layer l: hidden_{l+1} = round(sum of the ranks' partials + hidden_l)
+      if (!consumer_phase_wait(p.bar, static_cast<int>(gridDim.x) * (ph + 2), status, &s_abort)) break;
+      const T* res = static_cast<const T*>(gl == 0 ? p.hidden : p.ping[(gl - 1) & 1]);
+      T* out = static_cast<T*>(gl == p.total_layers - 1 ? p.out : p.ping[gl & 1]);
+      if (!tp_reduce_phase<T>(p, s_seq0 + l, res, out, status)) s_abort = 1;
+      phase_arrive(p.bar);
+      if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+    }
   }
 }
 
@@ -331,9 +406,9 @@ StackGeometry stack_geometry(int m, int64_t h, int64_t i, int nes, int grid) {
   return g;
 }
 
-template <typename T, int NT>
+template <typename T, int NT, bool TP>
 cudaError_t launch_stack(const StackParams& p, int grid, size_t smem, cudaStream_t st) {
-  auto kern = mlp_stack_kernel<T, NT>;
+  auto kern = mlp_stack_kernel<T, NT, TP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -355,11 +430,14 @@ namespace fd_host {
 
 // The persistent stack for `layers` layers (weights as arrays of device
 // pointers).  Returns FD_ERR_UNSUPPORTED when this shape is not served by the
-// persistent kernel (the caller then runs the two-launch chain).
+// persistent kernel (the caller then runs the launch chain).  With tp_world
+// > 0 the layers are tensor-parallel shards (i is this rank's share of the
+// intermediate width) and the partial sums travel through `exchange`.
 int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* norm_w, int32_t norm_dtype,
                          const void* const* w_gate_up, int64_t s_gu, const void* const* w_down, int64_t s_down,
                          void* out, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
-                         const fd_stream::Workspace& ws, void* mid, void* ping0, void* ping1, cudaStream_t st) {
+                         const fd_stream::Workspace& ws, void* mid, void* ping0, void* ping1, cudaStream_t st,
+                         int32_t tp_rank, int32_t tp_world, void* const* exchange, int32_t tp_mmax) {
   if (kind != FD_KIND_DOT || m < 1 || m > MT_MAX || layers < 1) return FD_ERR_UNSUPPORTED;
   if (std::getenv("FD_STACK_CHAIN")) return FD_ERR_UNSUPPORTED;
   const int nes = norm_dtype == FD_F32 ? 4 : 2;
@@ -388,6 +466,14 @@ int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* 
   da.total = da.nblocks * da.ks;
   da.slots = ws.slots; da.counters = ws.counters; da.status = ws.status;
   if (ga.nblocks > kMaxCounters || da.nblocks > kMaxCounters) return FD_ERR_UNSUPPORTED;
+  const bool tp = tp_world > 0;
+  if (tp) {
+    const TpLayout lay = tp_layout(tp_world, tp_mmax, h);
+    for (int k = 0; k < tp_world; ++k) da.tp_peer[k] = static_cast<char*>(exchange[k]);
+    da.tp_rank = tp_rank; da.tp_world = tp_world; da.tp_mmax = tp_mmax;
+    da.tp_data_off = lay.data_off;
+    p.tp_buf = static_cast<char*>(exchange[tp_rank]);
+  }
   p.hidden = hidden;
   p.out = out;
   p.ping[0] = static_cast<char*>(ping0);
@@ -409,10 +495,18 @@ int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* 
       p.norm_w[l] = norm_w[l0 + l];
     }
     cudaError_t e;
-    if (dtype == FD_BF16)
-      e = m <= 8 ? launch_stack<__nv_bfloat16, 1>(p, grid, geo.smem, st) : launch_stack<__nv_bfloat16, 2>(p, grid, geo.smem, st);
-    else
-      e = m <= 8 ? launch_stack<__half, 1>(p, grid, geo.smem, st) : launch_stack<__half, 2>(p, grid, geo.smem, st);
+    const bool wide = m > 8;
+    if (dtype == FD_BF16) {
+      if (tp) e = wide ? launch_stack<__nv_bfloat16, 2, true>(p, grid, geo.smem, st)
+                       : launch_stack<__nv_bfloat16, 1, true>(p, grid, geo.smem, st);
+      else e = wide ? launch_stack<__nv_bfloat16, 2, false>(p, grid, geo.smem, st)
+                    : launch_stack<__nv_bfloat16, 1, false>(p, grid, geo.smem, st);
+    } else {
+      if (tp) e = wide ? launch_stack<__half, 2, true>(p, grid, geo.smem, st)
+                       : launch_stack<__half, 1, true>(p, grid, geo.smem, st);
+      else e = wide ? launch_stack<__half, 2, false>(p, grid, geo.smem, st)
+                    : launch_stack<__half, 1, false>(p, grid, geo.smem, st);
+    }
     if (e != cudaSuccess) return FD_ERR_LAUNCH;
   }
   return FD_OK;

@@ -249,10 +249,9 @@ FD_DEV void st_tagged_sys(void* p, float v, int tag) {
 // rank's exchange buffer -- peers' through NVLink peer mappings -- as a word
 // tagged with the round number (layout: TpLayout).  No fence, no flag.
 template <int NT>
-FD_DEV void tp_publish(const GemvArgs& a, int64_t blk, const Acc<NT>& acc) {
+FD_DEV void tp_publish(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, int seq) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int seq = *reinterpret_cast<const volatile int*>(a.tp_seq);
   const int64_t slab = static_cast<int64_t>((seq & 1) * a.tp_world + a.tp_rank) * a.tp_mmax * a.n;
   for (int rk = 0; rk < a.tp_world; ++rk) {
     uint2* d = reinterpret_cast<uint2*>(a.tp_peer[rk] + a.tp_data_off) + slab;
@@ -298,7 +297,7 @@ struct Epilogue<T, NT, MODE_LINEAR> {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
     if (a.tp_world > 0) {
-      tp_publish(a, blk, acc);
+      tp_publish(a, blk, acc, *reinterpret_cast<const volatile int*>(a.tp_seq));
       return;
     }
 #pragma unroll
@@ -325,6 +324,7 @@ struct Epilogue<T, NT, MODE_LINEAR> {
 // registers in the streaming loop -- while the layer changes.
 __shared__ const void* sx_ra;  // LINEAR_X: the residual rows added in the epilogue
 __shared__ char* sx_y;         // LINEAR_X: the output rows
+__shared__ int sx_seq;         // LINEAR_X, tensor parallel: the layer's exchange round
 
 // LINEAR_X: y = round(acc + row_add), with row_add and y from sx_ra / sx_y
 // (the stack's down projection: no bias, 16-bit output).
@@ -340,12 +340,17 @@ struct Epilogue<T, NT, MODE_LINEAR_X> {
       for (int e = 0; e < 4; ++e) {
         const int64_t row = blk * BR + 16 * warp + g + 8 * (e >> 1);
         const int col = 8 * t + 2 * q + (e & 1);
-        ex.v[t][e] = (row < a.n && col < a.m) ? load_as_f32_cg(ra, a.ra_dtype, col * a.srm + row * a.srn) : 0.f;
+        ex.v[t][e] = (a.tp_world == 0 && row < a.n && col < a.m)
+                         ? load_as_f32_cg(ra, a.ra_dtype, col * a.srm + row * a.srn) : 0.f;
       }
   }
   FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& ex, float* /*xchg*/) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
+    if (a.tp_world > 0) {  // tensor parallel: the fp32 partial goes to every rank's exchange buffer
+      tp_publish(a, blk, acc, sx_seq);
+      return;
+    }
     T* y = reinterpret_cast<T*>(sx_y);
 #pragma unroll
     for (int t = 0; t < NT; ++t)
@@ -1178,6 +1183,8 @@ namespace fd_host {
 int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* norm_w, int32_t norm_dtype,
                          const void* const* w_gate_up, int64_t s_gu, const void* const* w_down, int64_t s_down,
                          void* out, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
-                         const fd_stream::Workspace& ws, void* mid, void* ping0, void* ping1, cudaStream_t st);
+                         const fd_stream::Workspace& ws, void* mid, void* ping0, void* ping1, cudaStream_t st,
+                         int32_t tp_rank = 0, int32_t tp_world = 0, void* const* exchange = nullptr,
+                         int32_t tp_mmax = 0);
 int mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i, int32_t kind);
 }  // namespace fd_host

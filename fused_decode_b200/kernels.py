@@ -393,6 +393,47 @@ def post_attn_mlp_tp_out(
     _capi.check(status, "fd_post_attn_mlp_tp_out")
 
 
+def post_attn_mlp_tp_stack_out(
+    hidden2: torch.Tensor,
+    layers,
+    out2: torch.Tensor,
+    eps: float,
+    kind: str,
+    exchange,
+) -> None:
+    """``len(layers)`` tensor-parallel MLP layers ``(norm_weight, w_gate_up
+    shard, w_down shard)`` enqueued by one library call: one persistent
+    kernel per 32 layers (kind "dot") whose partial sums travel through the
+    NVLink exchange buffers of ``exchange``; the last output lands in ``out2``
+    on every rank."""
+    if not layers:
+        raise ValueError("need at least one layer")
+    m, h = hidden2.shape
+    nw0, wgu0, wd0 = layers[0]
+    i = wd0.shape[1]
+    if m > exchange.m_max:
+        raise ValueError(f"batch {m} exceeds the exchange's m_max={exchange.m_max}")
+    if h != exchange.hidden:
+        raise ValueError(f"hidden width {h} does not match the exchange's {exchange.hidden}")
+    for nw, wgu, wd in layers:
+        if (wgu.shape != wgu0.shape or wd.shape != wd0.shape or wgu.stride() != wgu0.stride()
+                or wd.stride() != wd0.stride() or nw.dtype != nw0.dtype or nw.shape != nw0.shape):
+            raise ValueError("all layers must share shapes, strides and dtypes")
+    lib = _capi.load()
+    ws = WORKSPACES.get(hidden2.device, lib.fd_post_attn_mlp_workspace_bytes(m, h, i))
+    status = lib.fd_post_attn_mlp_tp_stack_out(
+        hidden2.data_ptr(), len(layers),
+        _capi.ptr_array([nw.data_ptr() for nw, _, _ in layers]), _capi.dtype_code(nw0.dtype),
+        _capi.ptr_array([wgu.data_ptr() for _, wgu, _ in layers]), int(wgu0.stride(0)),
+        _capi.ptr_array([wd.data_ptr() for _, _, wd in layers]), int(wd0.stride(0)),
+        out2.data_ptr(), _capi.dtype_code(hidden2.dtype), m, h, i, float(eps),
+        _capi.FD_KIND_DOT if kind == "dot" else _capi.FD_KIND_SIMT,
+        exchange.rank, exchange.world, exchange.pointers, exchange.m_max,
+        ws.data_ptr(), ws.numel(), _capi.stream_of(hidden2),
+    )
+    _capi.check(status, "fd_post_attn_mlp_tp_stack_out")
+
+
 def mlp_gate_up_out(
     hidden2: torch.Tensor,
     norm_weight: torch.Tensor,

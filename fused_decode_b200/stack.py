@@ -5,8 +5,11 @@ to take host launch cost out of the step.  ``MlpStack`` is that as a reusable
 object: it captures the whole stack on a private stream, and ``__call__``
 copies the input into the graph's static buffer, replays, and returns the
 static output.  By default the whole stack is enqueued by one library call
-(``fd_post_attn_mlp_stack_out``: two programmatic-dependent launches per
-layer, intermediates in the library workspace).  ``fused=False`` captures one
+(``fd_post_attn_mlp_stack_out``: one persistent kernel per 32 layers for
+kind "dot", else two programmatic-dependent launches per layer;
+intermediates in the library workspace).  With ``exchange=`` (a
+``fused_decode_b200.tp.TPExchange``) the layers are this rank's
+tensor-parallel shards and the call is ``fd_post_attn_mlp_tp_stack_out``.  ``fused=False`` captures one
 ``post_attn_mlp`` call per layer instead, and ``layer_fn`` captures any per-layer callable (the
 tensor-parallel layer of ``fused_decode_b200.tp``, for one).
 """
@@ -39,6 +42,7 @@ class MlpStack:
         kind: str | None = None,
         layer_fn=None,
         fused: bool | None = None,
+        exchange=None,
     ) -> None:
         if not layers:
             raise ValueError("need at least one layer")
@@ -50,7 +54,16 @@ class MlpStack:
         self.h = int(wgu0.shape[1])
         self.device = wgu0.device
         self.dtype = wgu0.dtype
-        self._fn = layer_fn or (lambda x, nw, wgu, wd: post_attn_mlp(x, nw, wgu, wd, self.eps, kind=self.kind))
+        self.exchange = exchange
+        if layer_fn is None and exchange is not None:
+            from fused_decode_b200 import tp
+
+            def layer_fn_tp(x, nw, wgu, wd):
+                return tp.TPPostAttnMlp(nw, wgu, wd, self.eps, kind=self.kind, exchange=exchange)(x)
+
+            self._fn = layer_fn_tp
+        else:
+            self._fn = layer_fn or (lambda x, nw, wgu, wd: post_attn_mlp(x, nw, wgu, wd, self.eps, kind=self.kind))
         self.static_in = torch.zeros(batch, self.h, device=self.device, dtype=self.dtype)
         can_fuse = layer_fn is None and all(
             K.mlp_fusable(self.static_in, nw, wgu, wd) for nw, wgu, wd in self.layers)
@@ -64,7 +77,10 @@ class MlpStack:
     def _run(self, x: torch.Tensor) -> torch.Tensor:
         if self.fused:
             out = torch.empty_like(x)
-            K.post_attn_mlp_stack_out(x, self.layers, out, self.eps, self.kind)
+            if self.exchange is not None:
+                K.post_attn_mlp_tp_stack_out(x, self.layers, out, self.eps, self.kind, self.exchange)
+            else:
+                K.post_attn_mlp_stack_out(x, self.layers, out, self.eps, self.kind)
             return out
         for nw, wgu, wd in self.layers:
             x = self._fn(x, nw, wgu, wd)
@@ -84,12 +100,14 @@ class MlpStack:
     def launches_per_replay(self) -> int:
         """Kernel launches of this library per replay: one persistent kernel
         per 32 layers where the stack entry point runs one, else two per layer."""
+        per_layer = 3 if self.exchange is not None else 2
         if not self.fused:
-            return 2 * len(self.layers)
+            return per_layer * len(self.layers)
         nw0, wgu0, wd0 = self.layers[0]
-        return int(_capi.load().fd_post_attn_mlp_stack_launches(
+        n = int(_capi.load().fd_post_attn_mlp_stack_launches(
             len(self.layers), _capi.dtype_code(nw0.dtype), int(self.static_in.shape[0]), self.h,
             int(wd0.shape[1]), _capi.FD_KIND_DOT if self.kind == "dot" else _capi.FD_KIND_SIMT))
+        return n if n < 2 * len(self.layers) else per_layer * len(self.layers)
 
     def replay(self) -> torch.Tensor:
         self.graph.replay()

@@ -241,6 +241,25 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
                             void* const* exchange, int32_t m_max,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* `layers` consecutive tensor-parallel post_attn_mlp layers on rank `rank`
+ * of `world` (no counterpart in the reference): the stack form of
+ * fd_post_attn_mlp_tp_out, with norm_w, w_gate_up (this rank's [2*i, h]
+ * restacks) and w_down (its [h, i] column slices) as HOST arrays of device
+ * pointers; only the last layer's output is written to `out`, every rank
+ * getting the same bits.  kind = FD_KIND_DOT runs it as one persistent
+ * cooperative kernel per 32 layers -- per layer a gate/up phase, a down
+ * phase whose block partials go to every rank's exchange buffer, and a
+ * phase that sums the ranks' partials (bounded waits, status bit 8) and adds
+ * the residual -- with no launch between layers; otherwise three launches
+ * per layer.  The same exchange and round-counting rules as
+ * fd_post_attn_mlp_tp_out.  Workspace: fd_post_attn_mlp_workspace_bytes(m, h, i). */
+int fd_post_attn_mlp_tp_stack_out(const void* hidden, int32_t layers, const void* const* norm_w,
+                                  int32_t norm_dtype, const void* const* w_gate_up, int64_t s_gu,
+                                  const void* const* w_down, int64_t s_down, void* out, int32_t dtype,
+                                  int32_t m, int64_t h, int64_t i, float eps, int32_t kind, int32_t rank,
+                                  int32_t world, void* const* exchange, int32_t m_max, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* First kernel of fd_post_attn_mlp_out on its own: mid[m, i] (contiguous) =
  * round(silu(gate) * up) of the RMSNorm'd hidden rows.  Replaces the
  * rms_norm -> linear_decode -> swiglu launches of post_attn_mlp (reference

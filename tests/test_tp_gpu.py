@@ -272,3 +272,105 @@ def test_tp_nvlink_layers():
         x = x0 if x is None else x
         x = O.post_attn_mlp(x, nw, wgu, wd, EPS, "bfloat16")
     torch.testing.assert_close(torch.from_numpy(outs[0]), torch.from_numpy(x), **TOL)
+
+
+@pytest.mark.parametrize("m", [1, 8])
+def test_tp_stack_single_rank(m):
+    """The tensor-parallel stack entry point (one persistent kernel: gate/up,
+    down with the partials published into the exchange buffer, reduce) with a
+    group of one: the same bits as per-layer calls, replay after replay in a
+    CUDA graph (the exchange rounds advance), each layer within the parity bar
+    of the oracle on its own input, and the per-layer exchange path still in
+    step with the round number afterwards."""
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200 import post_attn_mlp
+    from fused_decode_b200.stack import MlpStack
+
+    h, i, layers = 1024, 2816, 4
+    ex = tp.TPExchange(h, m_max=16)
+    try:
+        ws = [_layer(h, i, m, 960 + l)[1:] for l in range(layers)]
+        x0 = _layer(h, i, m, 990)[0]
+        out = torch.empty_like(x0)
+        K.post_attn_mlp_tp_stack_out(x0, ws, out, EPS, "dot", ex)
+        x = x0
+        for nw, wgu, wd in ws:
+            y = post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot")
+            torch.testing.assert_close(y.float().cpu(), torch.from_numpy(
+                O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), EPS, "bfloat16")), **TOL)
+            x = y
+        assert torch.equal(out, x)
+        stack = MlpStack(ws, m, EPS, kind="dot", exchange=ex)
+        assert stack.launches_per_replay == 1
+        for _ in range(3):
+            assert torch.equal(stack(x0), x)
+        assert torch.equal(tp.TPPostAttnMlp(*ws[0], EPS, kind="dot", exchange=ex)(x0),
+                           post_attn_mlp(x0, *ws[0], EPS, kind="dot"))
+        torch.cuda.synchronize()
+        assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+    finally:
+        ex.close()
+
+
+def _rank_main_tp_stack(rank, world, port, outdir, h, i, m, layers):
+    import torch.distributed as dist
+
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200.stack import MlpStack
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ex = None
+    try:
+        dev = torch.device("cuda", rank)
+        ex = tp.TPExchange(h, m_max=16)
+        shards, x0 = [], None
+        for layer in range(layers):
+            xl, nw, wgu, wd = _layer(h, i, m, 500 + layer, device=dev)
+            x0 = xl if x0 is None else x0
+            shards.append((nw, tp.shard_gate_up(wgu, rank, world), tp.shard_down(wd, rank, world)))
+        out = torch.empty_like(x0)
+        K.post_attn_mlp_tp_stack_out(x0, shards, out, EPS, "dot", ex)  # one persistent kernel
+        x = x0
+        for nw, wgu, wd in shards:  # three launches per layer
+            x = tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)(x)
+        stack = MlpStack(shards, m, EPS, kind="dot", exchange=ex)
+        g = [stack(x0).clone() for _ in range(2)]
+        torch.cuda.synchronize()
+        np.save(os.path.join(outdir, f"rank{rank}.npy"),
+                np.stack([_np(out), _np(x), _np(g[0]), _np(g[1])]))
+        dist.barrier()
+        del stack
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_tp_stack_nvlink():
+    """The persistent tensor-parallel stack on 2..8 GPUs: on every rank the
+    same bits as the per-layer NVLink path and as its own graph replays, and
+    equal across ranks; the chain matches the unsharded oracle chain."""
+    import torch.multiprocessing as mp
+
+    h, i, m, layers = 1024, 2816, 4, 3
+    world = min(torch.cuda.device_count(), 8)
+    while (i % world or (i // world) % 8) and world > 2:
+        world -= 1
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rank_main_tp_stack, args=(world, _free_port(), d, h, i, m, layers), nprocs=world,
+                           join=True, start_method="spawn")
+        outs = [np.load(os.path.join(d, f"rank{r}.npy")) for r in range(world)]
+    for o in outs:
+        assert np.array_equal(o[0], o[1]) and np.array_equal(o[0], o[2]) and np.array_equal(o[0], o[3])
+        assert np.array_equal(o[0], outs[0][0])
+    x = None
+    for layer in range(layers):
+        x0, nw, wgu, wd = [_np(t) for t in _layer(h, i, m, 500 + layer, device="cpu")]
+        x = x0 if x is None else x
+        x = O.post_attn_mlp(x, nw, wgu, wd, EPS, "bfloat16")
+    torch.testing.assert_close(torch.from_numpy(outs[0][0]), torch.from_numpy(x), rtol=2e-2, atol=2e-2)
