@@ -683,6 +683,8 @@ def run_ours(args) -> None:
         return tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=exchange)(x)
 
     def build_stack(m):
+        if world > 1 and exchange is not None:  # one persistent kernel: gate/up, down, NVLink reduce
+            return MlpStack(layers, m, EPS, kind="dot", exchange=exchange)
         fn = layer_fn_tp if world > 1 else None
         return MlpStack(layers, m, EPS, kind="dot", layer_fn=fn)
 
@@ -893,9 +895,10 @@ def run_ours(args) -> None:
                     "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
                     "api": "fused_decode_b200.stack.MlpStack (pinned host in, graph replay, pinned host out)",
                     "eager_api_us_per_layer": e2e_eager_s * 1e6 / LAYERS},
-            # single GPU: two launches per layer; tensor-parallel: gate/up, down
-            # and reduce (NVLink exchange) or residual-add (after NCCL) per layer
-            "gpu_launches": args.steps * (stack1.launches_per_replay if world == 1 else 3 * LAYERS),
+            # one persistent kernel per 32 layers (single GPU, or tensor parallel
+            # over the NVLink exchange); with NCCL: gate/up, down and residual-add per layer
+            "gpu_launches": args.steps * (3 * LAYERS if world > 1 and exchange is None
+                                          else stack1.launches_per_replay),
             "tp_collective": args.tp_collective if world > 1 else None,
             "clocks": clocks,
         }
