@@ -428,6 +428,22 @@ cudaError_t launch_stack(const StackParams& p, int grid, size_t smem, cudaStream
 
 namespace fd_host {
 
+// Whether a stack runs as the persistent kernel.  Measured on B200 (32-layer
+// Llama-3-8B stacks, CUDA graphs): on one GPU the two-launch chain is as fast
+// or faster at every batch (M=1 66.4 vs 70.4 us/layer, M=8 72.3 vs 82.1) --
+// a phase boundary inside the kernel costs what a kernel boundary costs, the
+// skew of the slowest SM and the activation round trips, while the chain's
+// gate/up and down launches each get a ring sized for their own phase -- so
+// there the persistent kernel is opt-in (FD_STACK_PERSISTENT=1).  Tensor
+// parallel stacks use it by default: it folds the rank reduction into the
+// kernel, three launches per layer fewer.  It needs at least 4 ring stages.
+bool persistent_wanted(bool tp, const StackGeometry& geo) {
+  if (geo.stages < 4) return false;
+  if (tp) return true;
+  const char* env = std::getenv("FD_STACK_PERSISTENT");
+  return env && env[0] == '1';
+}
+
 // The persistent stack for `layers` layers (weights as arrays of device
 // pointers).  Returns FD_ERR_UNSUPPORTED when this shape is not served by the
 // persistent kernel (the caller then runs the launch chain).  With tp_world
@@ -439,11 +455,10 @@ int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* 
                          const fd_stream::Workspace& ws, void* mid, void* ping0, void* ping1, cudaStream_t st,
                          int32_t tp_rank, int32_t tp_world, void* const* exchange, int32_t tp_mmax) {
   if (kind != FD_KIND_DOT || m < 1 || m > MT_MAX || layers < 1) return FD_ERR_UNSUPPORTED;
-  if (std::getenv("FD_STACK_CHAIN")) return FD_ERR_UNSUPPORTED;
   const int nes = norm_dtype == FD_F32 ? 4 : 2;
   const int grid = sm_count();
   const StackGeometry geo = stack_geometry(m, h, i, nes, grid);
-  if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
+  if (!persistent_wanted(tp_world > 0, geo)) return FD_ERR_UNSUPPORTED;
 
   StackParams p;
   std::memset(&p, 0, sizeof(p));
@@ -514,12 +529,22 @@ int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* 
 
 int mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i, int32_t kind) {
   if (layers <= 0 || m <= 0 || h <= 0) return 0;
-  const bool persistent = kind == FD_KIND_DOT && m <= MT_MAX && !std::getenv("FD_STACK_CHAIN") &&
-                          stack_geometry(m, h, i, norm_dtype == FD_F32 ? 4 : 2, sm_count()).stages > 0;
+  const bool persistent =
+      kind == FD_KIND_DOT && m <= MT_MAX &&
+      persistent_wanted(false, stack_geometry(m, h, i, norm_dtype == FD_F32 ? 4 : 2, sm_count()));
   return persistent ? (layers + kStackMaxLayers - 1) / kStackMaxLayers : 2 * layers;
 }
 
 }  // namespace fd_host
+
+extern "C" int fd_post_attn_mlp_tp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h,
+                                                  int64_t i, int32_t kind) {
+  if (layers <= 0 || m <= 0 || h <= 0) return 0;
+  const bool persistent =
+      kind == FD_KIND_DOT && m <= MT_MAX &&
+      fd_host::persistent_wanted(true, stack_geometry(m, h, i, norm_dtype == FD_F32 ? 4 : 2, fd_host::sm_count()));
+  return persistent ? (layers + kStackMaxLayers - 1) / kStackMaxLayers : 3 * layers;
+}
 
 extern "C" int fd_post_attn_mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,
                                                int32_t kind) {

@@ -5,8 +5,8 @@ to take host launch cost out of the step.  ``MlpStack`` is that as a reusable
 object: it captures the whole stack on a private stream, and ``__call__``
 copies the input into the graph's static buffer, replays, and returns the
 static output.  By default the whole stack is enqueued by one library call
-(``fd_post_attn_mlp_stack_out``: one persistent kernel per 32 layers for
-kind "dot", else two programmatic-dependent launches per layer;
+(``fd_post_attn_mlp_stack_out``: two programmatic-dependent launches per
+layer, or one persistent kernel per 32 layers with FD_STACK_PERSISTENT=1;
 intermediates in the library workspace).  With ``exchange=`` (a
 ``fused_decode_b200.tp.TPExchange``) the layers are this rank's
 tensor-parallel shards and the call is ``fd_post_attn_mlp_tp_stack_out``.  ``fused=False`` captures one
@@ -99,15 +99,19 @@ class MlpStack:
     @property
     def launches_per_replay(self) -> int:
         """Kernel launches of this library per replay: one persistent kernel
-        per 32 layers where the stack entry point runs one, else two per layer."""
+        per 32 layers where the stack entry point runs one, else two per layer
+        (three per layer for a tensor-parallel stack)."""
         per_layer = 3 if self.exchange is not None else 2
         if not self.fused:
             return per_layer * len(self.layers)
         nw0, wgu0, wd0 = self.layers[0]
-        n = int(_capi.load().fd_post_attn_mlp_stack_launches(
+        if self.exchange is not None:
+            return int(_capi.load().fd_post_attn_mlp_tp_stack_launches(
+                len(self.layers), _capi.dtype_code(nw0.dtype), int(self.static_in.shape[0]), self.h,
+                int(wd0.shape[1]), _capi.FD_KIND_DOT if self.kind == "dot" else _capi.FD_KIND_SIMT))
+        return int(_capi.load().fd_post_attn_mlp_stack_launches(
             len(self.layers), _capi.dtype_code(nw0.dtype), int(self.static_in.shape[0]), self.h,
             int(wd0.shape[1]), _capi.FD_KIND_DOT if self.kind == "dot" else _capi.FD_KIND_SIMT))
-        return n if n < 2 * len(self.layers) else per_layer * len(self.layers)
 
     def replay(self) -> torch.Tensor:
         self.graph.replay()

@@ -185,15 +185,16 @@ int fd_post_attn_mlp_out(const void* hidden, const void* norm_w, int32_t norm_dt
  * pointers with shared shapes, strides and dtypes.  Intermediate activations
  * live in the workspace and only the last layer's output is written to
  * `out`.  The workspace is fd_post_attn_mlp_workspace_bytes(m, h, i).
- * kind = FD_KIND_DOT runs the stack as ONE persistent cooperative kernel per
- * 32 layers (one CTA per SM; the weight stream runs on across layer and
- * phase boundaries while grid-wide barriers order the activations; status
- * bit 16: a barrier wait expired); otherwise, or where the batch does not
- * fit its shared-memory plan, two launches per layer.  Both give the same
- * bits as one fd_post_attn_mlp_out call per layer.
+ * Two programmatic-dependent launches per layer.  With FD_STACK_PERSISTENT=1
+ * in the environment and kind = FD_KIND_DOT, ONE persistent cooperative
+ * kernel per 32 layers instead (one CTA per SM; the weight stream runs on
+ * across layer and phase boundaries while grid-wide barriers order the
+ * activations; status bit 16: a barrier wait expired) where the batch leaves
+ * it at least 4 ring stages -- measured no faster on one B200, so not the
+ * default.  Both give the same bits as one fd_post_attn_mlp_out call per layer.
  * Replaces a loop of post_attn_mlp calls (reference ops.py:283-315). */
 /* Kernel launches one fd_post_attn_mlp_stack_out call of this shape makes
- * (no counterpart in the reference). */
+ * under the current environment (no counterpart in the reference). */
 int fd_post_attn_mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,
                                     int32_t kind);
 int fd_post_attn_mlp_stack_out(const void* hidden, int32_t layers,
@@ -246,13 +247,17 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
  * fd_post_attn_mlp_tp_out, with norm_w, w_gate_up (this rank's [2*i, h]
  * restacks) and w_down (its [h, i] column slices) as HOST arrays of device
  * pointers; only the last layer's output is written to `out`, every rank
- * getting the same bits.  kind = FD_KIND_DOT runs it as one persistent
- * cooperative kernel per 32 layers -- per layer a gate/up phase, a down
+ * getting the same bits.  kind = FD_KIND_DOT (where the batch leaves at
+ * least 4 ring stages) runs it as one persistent cooperative kernel per 32 layers -- per layer a gate/up phase, a down
  * phase whose block partials go to every rank's exchange buffer, and a
  * phase that sums the ranks' partials (bounded waits, status bit 8) and adds
  * the residual -- with no launch between layers; otherwise three launches
  * per layer.  The same exchange and round-counting rules as
  * fd_post_attn_mlp_tp_out.  Workspace: fd_post_attn_mlp_workspace_bytes(m, h, i). */
+/* Kernel launches one fd_post_attn_mlp_tp_stack_out call of this shape makes
+ * (i: this rank's share of the intermediate width). */
+int fd_post_attn_mlp_tp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,
+                                       int32_t kind);
 int fd_post_attn_mlp_tp_stack_out(const void* hidden, int32_t layers, const void* const* norm_w,
                                   int32_t norm_dtype, const void* const* w_gate_up, int64_t s_gu,
                                   const void* const* w_down, int64_t s_down, void* out, int32_t dtype,
