@@ -731,6 +731,12 @@ def run_ours(args) -> None:
         ms_pl, _ = time_stack(stack_pl, max(3, args.steps // 5), args.warmup)
         per_layer_us = ms_pl * 1e3 / LAYERS
         del stack_pl
+    elif exchange is not None:
+        # tensor parallel: the per-layer path (gate/up, down, NVLink reduce: three launches a layer)
+        stack_pl = MlpStack(layers, args.m, EPS, kind="dot", layer_fn=layer_fn_tp)
+        ms_pl, _ = time_stack(stack_pl, max(3, args.steps // 5), args.warmup)
+        per_layer_us = ms_pl * 1e3 / LAYERS
+        del stack_pl
 
     # ---- the same stack as two stream-K kernels per layer (gate/up, then down + residual)
     two_kernel_us = None
