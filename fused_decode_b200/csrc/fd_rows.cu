@@ -385,73 +385,6 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a) {
   }
 }
 
-// Vector path when cos and sin broadcast over the innermost leading dimension
-// (stride 0 over it: the heads of [tokens, heads, head_dim] under
-// [tokens, 1, head_dim] tables, the usual RoPE call).  One thread takes one
-// 8-element column chunk of one (outer row, group of kHeadGroup heads): it
-// loads that chunk's cos/sin once and every head's x at once, so the angle
-// loads drop by kHeadGroup and all of the thread's x bytes are in flight in
-// one round trip.  Consecutive threads take consecutive chunks of a row
-// (coalesced 128-byte segments).
-constexpr int kHeadGroup = 8;
-
-template <typename T, typename CT>
-__global__ void __launch_bounds__(256, 2) rope_bcast_kernel(RopeArgs a) {
-  grid_dep_wait();
-  grid_dep_launch();
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t groups = (a.C + kHeadGroup - 1) / kHeadGroup;
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < a.items; it += stride) {
-    const int64_t jv = it % a.hv, rest = it / a.hv;
-    const int64_t g = rest % groups, rab = rest / groups;
-    const int64_t ib = rab % a.B, ia = rab / a.B;
-    const int64_t j = 8 * jv;
-    const CT* cp = reinterpret_cast<const CT*>(a.c.ptr) + (ia * a.c.sa + ib * a.c.sb);
-    const CT* sp = reinterpret_cast<const CT*>(a.s.ptr) + (ia * a.s.sa + ib * a.s.sb);
-    Angles8<CT> c1, c2, s1, s2;
-    c1.load(cp + j);
-    c2.load(cp + a.half + j);
-    s1.load(sp + j);
-    s2.load(sp + a.half + j);
-    const T* xb = reinterpret_cast<const T*>(a.x.ptr) + (ia * a.x.sa + ib * a.x.sb);
-    T* yb = reinterpret_cast<T*>(a.y.ptr) + (ia * a.y.sa + ib * a.y.sb);
-    const int64_t h0 = g * kHeadGroup;
-    uint4 x1[kHeadGroup], x2[kHeadGroup];
-#pragma unroll
-    for (int h = 0; h < kHeadGroup; ++h) {
-      if (h0 + h < a.C) {
-        const T* xp = xb + (h0 + h) * a.x.sc;
-        x1[h] = ld_stream16(xp + j);
-        x2[h] = ld_stream16(xp + a.half + j);
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < kHeadGroup; ++h) {
-      if (h0 + h < a.C) {
-        const uint32_t xw1[4] = {x1[h].x, x1[h].y, x1[h].z, x1[h].w}, xw2[4] = {x2[h].x, x2[h].y, x2[h].z, x2[h].w};
-        uint32_t o1[4], o2[4];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const float2 a1 = unpack2<T>(xw1[w]), a2 = unpack2<T>(xw2[w]);
-          const float2 cc1 = c1.pair(w), cc2 = c2.pair(w), ss1 = s1.pair(w), ss2 = s2.pair(w);
-          o1[w] = pack2<T>(a1.x * cc1.x - a2.x * ss1.x, a1.y * cc1.y - a2.y * ss1.y);
-          o2[w] = pack2<T>(a2.x * cc2.x + a1.x * ss2.x, a2.y * cc2.y + a1.y * ss2.y);
-        }
-        T* yp = yb + (h0 + h) * a.y.sc;
-        st_stream16(yp + j, make_uint4(o1[0], o1[1], o1[2], o1[3]));
-        st_stream16(yp + a.half + j, make_uint4(o2[0], o2[1], o2[2], o2[3]));
-      }
-    }
-  }
-}
-
-template <typename T>
-cudaError_t launch_rope_bcast(const RopeArgs& a, int cs_dtype, cudaStream_t st) {
-  if (cs_dtype == FD_F32) return launch_stream(rope_bcast_kernel<T, float>, a, a.items, st);
-  if (cs_dtype == FD_BF16) return launch_stream(rope_bcast_kernel<T, __nv_bfloat16>, a, a.items, st);
-  return launch_stream(rope_bcast_kernel<T, __half>, a, a.items, st);
-}
-
 template <typename T>
 __global__ void __launch_bounds__(256) rope_generic_kernel(RopeArgs a) {
   grid_dep_wait();
@@ -709,14 +642,6 @@ int fd_rope_out(const fd_rows* x, const fd_rows* cos, const fd_rows* sin, const 
   a.half = x->n / 2;
   const bool vec = a.half % 8 == 0 && cos->dtype == sin->dtype && rows_vec16(x) && rows_vec16(cos) &&
                    rows_vec16(sin) && rows_vec16(out);
-  if (vec && x->c > 1 && cos->sc == 0 && sin->sc == 0) {
-    // angles shared by every index of the innermost leading dimension (heads)
-    a.hv = a.half / 8;
-    a.items = x->a * x->b * ((x->c + kHeadGroup - 1) / kHeadGroup) * a.hv;
-    const cudaError_t e = bf ? launch_rope_bcast<__nv_bfloat16>(a, cos->dtype, st)
-                             : launch_rope_bcast<__half>(a, cos->dtype, st);
-    return from_cuda(e);
-  }
   if (vec) {
     a.hv = a.half / 8;
     a.items = rows * a.hv;
