@@ -341,3 +341,18 @@ def test_persistent_stack_two_launches(monkeypatch):
         for nw, wgu, wd in ws:
             x = post_attn_mlp(x, nw, wgu, wd, kind="dot")
         assert torch.equal(out, x)
+
+
+@pytest.mark.parametrize("m", [8, 16])
+def test_post_attn_mlp_llama70b_widths(m):
+    """Llama-3-70B widths (hidden 8192, intermediate 28672) through the fused
+    two-kernel MLP at the batches where the gate/up stage's shared memory is
+    tightest: the streamed batch keeps the ring deep and 16 rows fuse too."""
+    h, i = 8192, 28672
+    dtype = torch.bfloat16
+    nw, wgu, wd = _mlp_weights(h, i, dtype, 71)
+    x = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(72 + m))
+    assert K.mlp_fusable(x, nw, wgu, wd)
+    ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-5, "bfloat16")
+    for kind in ("dot", "simt"):
+        _close(post_attn_mlp(x, nw, wgu, wd, 1e-5, kind=kind), ref)
