@@ -997,17 +997,24 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
         }
       }
       // physical column 16q + 4h + j  <->  logical k of MMA h: (2q, 2q+1, 2q+8, 2q+9)
+      // The step's products are summed by the MMAs into a fresh accumulator,
+      // which is then added to the running sum with an fp32 add: an MMA adds
+      // its products into C with truncating alignment, so over K = 14336..28672
+      // a running C would lose low bits at every one of K/16 MMAs.
 #pragma unroll
-      for (int j = 0; j < MAX_BOXES; ++j) {
-        if (j < B) {
+      for (int t = 0; t < NT; ++t) {
+        float st[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            mma16816<T>(acc.v[t], wa[j][0].x, wb[j][0].x, wa[j][0].y, wb[j][0].y, xa[j][t][0].x, xa[j][t][0].y);
-            mma16816<T>(acc.v[t], wa[j][0].z, wb[j][0].z, wa[j][0].w, wb[j][0].w, xa[j][t][0].z, xa[j][t][0].w);
-            mma16816<T>(acc.v[t], wa[j][1].x, wb[j][1].x, wa[j][1].y, wb[j][1].y, xa[j][t][1].x, xa[j][t][1].y);
-            mma16816<T>(acc.v[t], wa[j][1].z, wb[j][1].z, wa[j][1].w, wb[j][1].w, xa[j][t][1].z, xa[j][t][1].w);
+        for (int j = 0; j < MAX_BOXES; ++j) {
+          if (j < B) {
+            mma16816<T>(st, wa[j][0].x, wb[j][0].x, wa[j][0].y, wb[j][0].y, xa[j][t][0].x, xa[j][t][0].y);
+            mma16816<T>(st, wa[j][0].z, wb[j][0].z, wa[j][0].w, wb[j][0].w, xa[j][t][0].z, xa[j][t][0].w);
+            mma16816<T>(st, wa[j][1].x, wb[j][1].x, wa[j][1].y, wb[j][1].y, xa[j][t][1].x, xa[j][t][1].y);
+            mma16816<T>(st, wa[j][1].z, wb[j][1].z, wa[j][1].w, wb[j][1].w, xa[j][t][1].z, xa[j][t][1].w);
           }
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc.v[t][e] += st[e];
       }
     } else {
 #pragma unroll

@@ -347,7 +347,15 @@ def test_persistent_stack_two_launches(monkeypatch):
 def test_post_attn_mlp_llama70b_widths(m):
     """Llama-3-70B widths (hidden 8192, intermediate 28672) through the fused
     two-kernel MLP at the batches where the gate/up stage's shared memory is
-    tightest: the streamed batch keeps the ring deep and 16 rows fuse too."""
+    tightest: the streamed batch keeps the ring deep and 16 rows fuse too.
+
+    Tolerance: the reference's own for its linear paths in bf16 (rtol = atol =
+    4e-2, its tests/test_ops.py:27-35).  The reference rounds gate_up and mid
+    to bf16; at these widths any fp32 summation order (this kernel's, or the
+    CPU oracle's) moves about 2 % of the 28672 mid values by one bf16 step,
+    and the down projection sums those steps: the oracle's own down
+    projection applied to this kernel's mid reproduces its output (checked
+    below), so the down stage adds no error of its own."""
     h, i = 8192, 28672
     dtype = torch.bfloat16
     nw, wgu, wd = _mlp_weights(h, i, dtype, 71)
@@ -355,4 +363,8 @@ def test_post_attn_mlp_llama70b_widths(m):
     assert K.mlp_fusable(x, nw, wgu, wd)
     ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-5, "bfloat16")
     for kind in ("dot", "simt"):
-        _close(post_attn_mlp(x, nw, wgu, wd, 1e-5, kind=kind), ref)
+        y = post_attn_mlp(x, nw, wgu, wd, 1e-5, kind=kind)
+        _close(y, ref, {"rtol": 4e-2, "atol": 4e-2})
+        mid = torch.empty(m, i, device="cuda", dtype=dtype)
+        K.mlp_gate_up_out(x, nw, wgu, mid, 1e-5, kind)
+        _close(y, O.linear(_np(mid), _np(wd), row_add=_np(x), dtype="bfloat16"))
