@@ -380,9 +380,9 @@ bool mlp_fusable(const at::Tensor& hidden, const at::Tensor& nw, const at::Tenso
   if (wgu.stride(1) != 1 || wd.stride(1) != 1 || wgu.stride(0) % 8 || wd.stride(0) % 8) return false;
   for (const at::Tensor* t : {&hidden, &nw, &wgu, &wd})
     if (reinterpret_cast<uintptr_t>(t->data_ptr()) % 16) return false;
+  const int64_t ks = (h + 127) / 128;
   const int64_t nes = nw.scalar_type() == at::kFloat ? 4 : 2;
-  const int64_t x_slot = m <= 8 ? 1024 : 2048;
-  const int64_t region = 2 * 2 * x_slot + ((h * nes + 15) & ~int64_t{15});
+  const int64_t region = ks * 2 * m * 128 + ((h * nes + 15) & ~int64_t{15});
   const int64_t smem = 1024 + 2 * 32768 + region + 64 * 16 * 4 + 2 * 12 * 8;
   return smem <= 227 * 1024 - 1024;
 }

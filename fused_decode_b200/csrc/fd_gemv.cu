@@ -27,18 +27,17 @@ __global__ void __launch_bounds__(MAXT, MINB)
   __shared__ __align__(8) uint64_t s_mid[2];
   __shared__ __align__(8) uint64_t s_nw_bar;  // norm weight copy landed (GATEUP)
   __shared__ int s_mid_last, s_fast, s_decided;
-  __shared__ float s_inv[MT_MAX];  // GATEUP: 1 / rms of each batch row
   const int nes = a.norm_dtype == FD_F32 ? 4 : 2;
-  const int64_t xbytes = MODE == MODE_GATEUP ? static_cast<int64_t>(gateup_stream_bytes(a.m, a.stages, a.boxes, a.k, nes))
+  const int64_t xbytes = MODE == MODE_GATEUP ? static_cast<int64_t>(gateup_region_bytes(a.m, a.ks, a.boxes, a.k, nes))
                                              : static_cast<int64_t>(a.stages) * a.boxes * a.x_slot;
-  Ring r = carve_ring(smem_raw, a.stages, a.boxes, a.x_slot, xbytes);
+  const Ring r = carve_ring(smem_raw, a.stages, a.boxes, a.x_slot, xbytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = static_cast<int>(blockDim.x >> 5) - GW - 1;  // warps: consumers, producers, announcer
   const int64_t G = gridDim.x, c = blockIdx.x;
   const int64_t s0 = range_start(c, a.total, G);
   const int64_t s1 = range_start(c + 1, a.total, G);
   const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided, 0u, 1};
-  unsigned char* nw_smem = r.xreg + static_cast<int64_t>(a.stages) * a.boxes * a.x_slot;  // GATEUP: norm weight copy
+  unsigned char* nw_smem = r.xreg + gateup_x_bytes(a.m, a.ks, a.boxes);  // GATEUP: norm weight copy
 
   if (threadIdx.x == 0) {
     mbar_init(&s_mid[0], GW);
@@ -74,7 +73,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
         bulk_load(nw_smem, a.norm_w, nb, &s_nw_bar);
       }
       prefetch_map(&wmap);
-      prefetch_map(&xmap);
+      if (MODE == MODE_LINEAR) prefetch_map(&xmap);
       produce_phase<MODE>(r, &wmap, &xmap, a, s0, s1, 0, p, P, evict_first_policy(), &s_abort, [] {
         grid_dep_wait();  // the activation is the previous kernel's output
         return true;
@@ -86,13 +85,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
   }
   // consumer warps
   grid_dep_wait();
-  if (MODE == MODE_GATEUP) {
-    // each row's 1/rms now; the rows themselves arrive box by box with the weights
-    norm_to_smem<T, true>(a, a.hidden, r, s_sumsq, nw_smem, &s_nw_bar, 0, s_inv);
-    if (!mbar_wait(&s_nw_bar, 0)) atomicOr(a.status, kStatusFullTimeout);
-    r.nw = nw_smem;
-    r.inv = s_inv;
-  }
+  if (MODE == MODE_GATEUP) norm_to_smem<T>(a, a.hidden, r, s_sumsq, nw_smem, &s_nw_bar);
   grid_dep_launch();
   consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort, ms);
 }
@@ -214,8 +207,9 @@ int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, c
                    int64_t s_gu, void* mid, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
                    const Workspace& ws, cudaStream_t st) {
   const int nes = norm_dtype == FD_F32 ? 4 : 2;
-  const Geometry geo = choose_geometry([m, h, nes](int stages, int boxes) {
-    return gateup_stream_bytes(m, stages, boxes, h, nes);
+  const Geometry geo = choose_geometry([m, h, nes](int, int boxes) {
+    const int64_t ks = (h + static_cast<int64_t>(boxes) * KC - 1) / (static_cast<int64_t>(boxes) * KC);
+    return gateup_region_bytes(m, ks, boxes, h, nes);
   });
   if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
   GemvArgs a = {};
@@ -231,15 +225,11 @@ int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, c
   a.inner = i;
   a.hidden = hidden; a.hidden_stride = h;
   a.norm_w = norm_w; a.norm_dtype = norm_dtype; a.eps = eps;
-  a.x_slot = x_slot_bytes(m);
-  CUtensorMap gm, xm;
-  // A single row's stride is never used by the TMA unit; keep it legal.
-  const int64_t xstride = m == 1 ? ((h + 7) / 8) * 8 : h;
-  if (!make_gate_up_map(&gm, w_gate_up, h, i, s_gu) || !make_map_2d(&xm, hidden, m, h, xstride, m))
-    return FD_ERR_LAUNCH;
-  const size_t smem = ring_smem_bytes(gateup_stream_bytes(m, a.stages, a.boxes, h, nes), a.stages, a.boxes);
-  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, xm, a, kind, geo, smem, st)
-                                   : dispatch_tma<__half, MODE_GATEUP>(gm, xm, a, kind, geo, smem, st);
+  CUtensorMap gm;
+  if (!make_gate_up_map(&gm, w_gate_up, h, i, s_gu)) return FD_ERR_LAUNCH;
+  const size_t smem = ring_smem_bytes(gateup_region_bytes(m, a.ks, a.boxes, h, nes), a.stages, a.boxes);
+  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st)
+                                   : dispatch_tma<__half, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st);
   return from_cuda(e);
 }
 

@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
         prefetch_map(&p.gu[l]);
         prefetch_map(&p.dn[l]);
         const auto ready = [] { return true; };
-        if (!produce_phase<MODE_GATEUP_X>(r, &p.gu[l], &p.gu[l], ga, g0, g1, base, pi, P, pol, &s_abort, ready))
+        if (!produce_phase<MODE_GATEUP>(r, &p.gu[l], &p.gu[l], ga, g0, g1, base, pi, P, pol, &s_abort, ready))
           break;
         base += g1 - g0;
         if (!produce_phase<MODE_LINEAR_X>(r, &p.dn[l], &p.dn[l], da, d0, d1, base, pi, P, pol, &s_abort, ready))
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
     norm_to_smem<T>(ga, *reinterpret_cast<const void* volatile*>(&s_hidden), r, s_sumsq, nw_smem, &s_nw_full,
                     static_cast<uint32_t>(l & 1));
     if (threadIdx.x == 0) mbar_arrive(&s_nw_empty);
-    if (!consume_phase<T, NT, 0, 1, MODE_GATEUP_X>(ga, r, rng[0], rng[1], base, rng[4], blockIdx.x, &s_last,
+    if (!consume_phase<T, NT, 0, 1, MODE_GATEUP>(ga, r, rng[0], rng[1], base, rng[4], blockIdx.x, &s_last,
                                                  &s_abort, sync_for(ph)))
       break;
     base += rng[1] - rng[0];

@@ -61,22 +61,11 @@ constexpr int kStatusFullTimeout = 1;
 constexpr int kStatusEmptyTimeout = 2;
 
 // LINEAR: a GEMV whose activation boxes arrive by TMA with the weight boxes.
-// GATEUP: the MLP gate/up stage; the raw hidden boxes arrive by TMA with the
-// weight boxes (as LINEAR) and the consumers normalise them in registers
-// with per-row scales computed once in the prologue -- so the shared memory
-// a stage needs does not grow with the batch beyond one [m x 64] box per
-// weight box, and every batch keeps a deep ring.
+// GATEUP: the MLP gate/up stage; the normalised batch is held in shared memory.
 // LINEAR_X: a GEMV whose activation columns for the CTA's step range were
 // staged in shared memory by the consumers (the persistent MLP stack's down
 // projection: its activation is written inside the same kernel).
-// GATEUP_X: the gate/up stage with the whole normalised batch resident in
-// shared memory (the persistent stack, whose producers run ahead of the
-// activation and so cannot load it with the weights).
-enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2, MODE_GATEUP_X = 3 };
-template <int MODE>
-__host__ __device__ constexpr bool gate_up_mode() { return MODE == MODE_GATEUP || MODE == MODE_GATEUP_X; }
-template <int MODE>
-__host__ __device__ constexpr bool x_by_tma() { return MODE == MODE_LINEAR || MODE == MODE_GATEUP; }
+enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2 };
 
 // One phase of streaming: a GEMV (LINEAR) or the MLP gate/up stage (GATEUP).
 struct GemvArgs {
@@ -414,9 +403,6 @@ struct Epilogue<T, NT, MODE_GATEUP> {
   }
 };
 
-template <typename T, int NT>
-struct Epilogue<T, NT, MODE_GATEUP_X> : Epilogue<T, NT, MODE_GATEUP> {};
-
 // Split-K bookkeeping.  A CTA's range [s0, s1) holds at most two blocks it
 // does not cover whole: the block it starts inside (slot 0) and the block it
 // ends inside (slot 1).  Their partials go to the CTA's two slots with plain
@@ -591,8 +577,6 @@ struct Ring {
   uint64_t* empty;
   int S, B, x_slot;
   int64_t w_stage;
-  const unsigned char* nw;  // GATEUP: the norm weight's copy in shared memory
-  const float* inv;         // GATEUP: 1 / rms of each batch row
 };
 
 FD_DEV Ring carve_ring(unsigned char* smem_raw, int S, int B, int x_slot, int64_t x_bytes) {
@@ -608,8 +592,6 @@ FD_DEV Ring carve_ring(unsigned char* smem_raw, int S, int B, int x_slot, int64_
   r.xchg = reinterpret_cast<float*>(r.xreg + ((x_bytes + 15) & ~15ll));
   r.full = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(r.xchg) + (BR / 2) * MT_MAX * 4);
   r.empty = r.full + MAX_STAGES;
-  r.nw = nullptr;
-  r.inv = nullptr;
   return r;
 }
 
@@ -623,7 +605,7 @@ FD_DEV void ring_init(const Ring& r) {
 
 template <int MODE>
 FD_DEV uint32_t stage_bytes(const Ring& r, const GemvArgs& a) {
-  return static_cast<uint32_t>(r.w_stage) + (x_by_tma<MODE>() ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
+  return static_cast<uint32_t>(r.w_stage) + (MODE == MODE_LINEAR ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
 }
 
 // Weight boxes of phase step t into ring index gi.
@@ -634,13 +616,13 @@ FD_DEV void issue_w(const Ring& r, const CUtensorMap* map, const GemvArgs& a, in
   unsigned char* dst = r.wst + s * r.w_stage;
   for (int j = 0; j < r.B; ++j) {
     const int32_t col = static_cast<int32_t>((kk * r.B + j) * KC);
-    if (gate_up_mode<MODE>())
+    if (MODE == MODE_GATEUP)
       tma_load_3d(dst + j * BOX_BYTES, map, col, static_cast<int32_t>(b * (BR / 2)), 0, &r.full[s], pol);
     else
       tma_load_2d(dst + j * BOX_BYTES, map, col, static_cast<int32_t>(b * BR), &r.full[s], pol);
   }
 }
-// Activation boxes (LINEAR, GATEUP) of phase step t into ring index gi.
+// Activation boxes (LINEAR) of phase step t into ring index gi.
 FD_DEV void issue_x(const Ring& r, const CUtensorMap* xmap, const GemvArgs& a, int64_t t, int64_t gi) {
   const int64_t kk = t - (t / a.ks) * a.ks;
   const int s = static_cast<int>(gi % r.S);
@@ -679,7 +661,7 @@ FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensor
     mbar_expect_tx(&r.full[gi % r.S], sb);
     issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
   }
-  if (x_by_tma<MODE>()) {
+  if (MODE == MODE_LINEAR) {
     if (!ready()) return false;
     for (int64_t g2 = first; g2 < base + npre; g2 += P) issue_x(r, xmap, a, s0 + (g2 - base), g2);
   }
@@ -687,7 +669,7 @@ FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensor
     if (!acquire(gi)) return false;
     mbar_expect_tx(&r.full[gi % r.S], sb);
     issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
-    if (x_by_tma<MODE>()) issue_x(r, xmap, a, s0 + (gi - base), gi);
+    if (MODE == MODE_LINEAR) issue_x(r, xmap, a, s0 + (gi - base), gi);
   }
   return true;
 }
@@ -729,18 +711,15 @@ FD_DEV void load8_smem_as_f32(const unsigned char* p, int dtype, float* f) {
 // split of the register batch folds away; 0 = rows too wide for one batch).
 // REGS: 16-byte vectors of hidden held per thread per group of rows.
 // NR: the exact row count when it is known at compile time (0: m at run time).
-template <typename T, int JV, int REGS = 8, int NR = 0, bool SCALES = false>
+template <typename T, int JV, int REGS = 8, int NR = 0>
 FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
-                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity, float* inv_out);
+                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity);
 
 // `hidden`: the rows to normalise (a.hidden for a single launch; the stack
-// passes each layer's input).  SCALES: only compute each row's 1/rms into
-// inv_out[m] (the streamed GATEUP mode normalises in registers); the norm
-// weight is not read and nothing goes to the X region.
-template <typename T, bool SCALES = false>
+// passes each layer's input).
+template <typename T>
 FD_DEV void norm_to_smem(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
-                         const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity = 0,
-                         float* inv_out = nullptr) {
+                         const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity = 0) {
   const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
   const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;
   // The prologue runs right after the launch, so its unrolled code is on the
@@ -750,33 +729,33 @@ FD_DEV void norm_to_smem(const GemvArgs& a, const void* hidden, const Ring& r, f
   // Other batches that fit four vectors per thread take the 4-vector group;
   // wider ones keep 8 vectors, so fewer groups (fewer load round trips).
   if (jv == 2 && a.m == 1) {
-    norm_rows<T, 2, 2, 1, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out);
+    norm_rows<T, 2, 2, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   if (jv == 2 && a.m == 2) {
-    norm_rows<T, 2, 4, 2, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out);
+    norm_rows<T, 2, 4, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   if (jv == 1 && a.m == 1) {
-    norm_rows<T, 1, 1, 1, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out);
+    norm_rows<T, 1, 1, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   if (jv == 1 && a.m <= 4) {
-    norm_rows<T, 1, 4, 0, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out);
+    norm_rows<T, 1, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
     return;
   }
   switch (jv) {
-    case 1: norm_rows<T, 1, 8, 0, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out); break;
-    case 2: norm_rows<T, 2, 8, 0, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out); break;
-    case 3: norm_rows<T, 3, 8, 0, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out); break;
-    case 4: norm_rows<T, 4, 8, 0, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out); break;
-    default: norm_rows<T, 0, 8, 0, SCALES>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity, inv_out); break;
+    case 1: norm_rows<T, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    case 2: norm_rows<T, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    case 3: norm_rows<T, 3>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    case 4: norm_rows<T, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+    default: norm_rows<T, 0>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
   }
 }
 
-template <typename T, int JV, int REGS, int NR, bool SCALES>
+template <typename T, int JV, int REGS, int NR>
 FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
-                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity, float* inv_out) {
+                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned char* xs = r.xreg;
   const int nvec = static_cast<int>(a.k / 8);
@@ -821,7 +800,7 @@ FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, floa
         }
       }
       consumer_sync();
-      if (!SCALES && r0 == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
+      if (r0 == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
       // one scale per row of the group, then a short loop over the vectors
       float inv[rows_per_group];
 #pragma unroll
@@ -830,15 +809,6 @@ FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, floa
 #pragma unroll
         for (int w = 0; w < GW; ++w) tot += s_sumsq[w][rr];
         inv[rr] = rr < nr ? rsqrtf(tot / static_cast<float>(a.k) + a.eps) : 0.f;  // rows past m: unused
-      }
-      if constexpr (SCALES) {
-        if (tid < nr) {
-#pragma unroll
-          for (int rr = 0; rr < rows_per_group; ++rr)
-            if (rr == tid) inv_out[r0 + rr] = inv[rr];
-        }
-        consumer_sync();  // s_sumsq is reused by the next group
-        continue;
       }
 #pragma unroll
       for (int e = 0; e < REGS; ++e) {
@@ -879,11 +849,6 @@ FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, floa
 #pragma unroll
     for (int w = 0; w < GW; ++w) tot += s_sumsq[w][0];
     const float inv = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
-    if constexpr (SCALES) {
-      if (tid == 0) inv_out[mrow] = inv;
-      consumer_sync();
-      continue;
-    }
     if (mrow == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
     for (int v = tid; v < nvec_pad; v += CONSUMERS) {
       uint4 packed = make_uint4(0, 0, 0, 0);
@@ -942,7 +907,7 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
     }
     // activation box j of this step: [m rows x 128 B] (swizzled by row & 7)
     auto xbox = [&](int j) -> const unsigned char* {
-      if (x_by_tma<MODE>()) return r.xreg + (s * B + j) * r.x_slot;
+      if (MODE == MODE_LINEAR) return r.xreg + (s * B + j) * r.x_slot;
       if (MODE == MODE_LINEAR_X) return r.xreg + ((it * B + j) * a.m) * 128;
       return r.xreg + ((ck * B + j) * a.m) * 128;
     };
@@ -967,35 +932,6 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&r.empty[s]);
-      if (MODE == MODE_GATEUP) {
-        // normed = round(x * inv_rms * w) (reference.py:14-18, rounded as
-        // reference.py:76 rounds `normed`): columns 16q .. 16q + 15 of box j
-#pragma unroll
-        for (int j = 0; j < MAX_BOXES; ++j) {
-          if (j < B) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int64_t col = (ck * B + j) * KC + 16 * q + 8 * h;
-              if (col < a.k) {
-                float w8[8];
-                load8_smem_as_f32(r.nw + col * (a.norm_dtype == FD_F32 ? 4 : 2), a.norm_dtype, w8);
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                  const int n = g + 8 * t;
-                  if (n < a.m) {
-                    const float inv = r.inv[n];
-                    float f[8];
-                    unpack8<T>(xa[j][t][h], f);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = f[e] * inv * w8[e];
-                    xa[j][t][h] = pack8<T>(f);
-                  }
-                }
-              }
-            }
-          }
-        }
-      }
       // physical column 16q + 4h + j  <->  logical k of MMA h: (2q, 2q+1, 2q+8, 2q+9)
       // The step's products are summed by the MMAs into a fresh accumulator,
       // which is then added to the running sum with an fp32 add: an MMA adds
@@ -1026,30 +962,12 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
           unpack8<T>(wb[j][0], wf[1]);
           unpack8<T>(wb[j][1], wf[1] + 8);
           const unsigned char* xt = xbox(j);
-          float w16[16];  // GATEUP: the norm weight of this lane's 16 columns (0 past k)
-          if (MODE == MODE_GATEUP) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int64_t col = (ck * B + j) * KC + 16 * q + 8 * h;
-              if (col < a.k) {
-                load8_smem_as_f32(r.nw + col * (a.norm_dtype == FD_F32 ? 4 : 2), a.norm_dtype, w16 + 8 * h);
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) w16[8 * h + e] = 0.f;
-              }
-            }
-          }
 #pragma unroll
           for (int mm = 0; mm < MP; ++mm) {
             if (mm < a.m) {
               float xf[16];
               unpack8<T>(*reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q)), xf);
               unpack8<T>(*reinterpret_cast<const uint4*>(xt + swz(mm, 2 * q + 1)), xf + 8);
-              if (MODE == MODE_GATEUP) {
-                const float inv = r.inv[mm];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) xf[e] = round_to<T>(xf[e] * inv * w16[e]);
-              }
 #pragma unroll
               for (int e = 0; e < 16; ++e) {
                 sacc[0][mm] = fmaf(wf[0][e], xf[e], sacc[0][mm]);
@@ -1098,7 +1016,7 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
         write_slot<NT>(a, 0, acc, c);
         __syncwarp();
         if (lane == 0) mbar_arrive(ms.ready);
-      } else if (gate_up_mode<MODE>() && head_of_final(s0, s1, a.ks)) {
+      } else if (MODE == MODE_GATEUP && head_of_final(s0, s1, a.ks)) {
         Acc<NT> ex;
         Epilogue<T, NT, MODE>::extras(a, cb, ex);
         if (threadIdx.x == 0) {
@@ -1220,13 +1138,7 @@ __host__ __device__ inline int x_slot_bytes(int m) { return m <= 8 ? 1024 : 2048
 __host__ __device__ inline size_t gateup_x_bytes(int m, int64_t ks, int boxes) {
   return static_cast<size_t>(ks) * boxes * m * 128;
 }
-// The streamed gate/up X region: S x B activation box slots (as LINEAR), then
-// the norm weight's copy.
-__host__ __device__ inline size_t gateup_stream_bytes(int m, int stages, int boxes, int64_t k, int norm_es) {
-  return static_cast<size_t>(stages) * boxes * x_slot_bytes(m) +
-         ((static_cast<size_t>(k) * norm_es + 15) & ~static_cast<size_t>(15));
-}
-// The resident gate/up X region (GATEUP_X): the normalised batch, then the norm weight's copy.
+// The gate/up X region: the normalised batch, then the norm weight's copy.
 __host__ __device__ inline size_t gateup_region_bytes(int m, int64_t ks, int boxes, int64_t k, int norm_es) {
   return gateup_x_bytes(m, ks, boxes) + ((static_cast<size_t>(k) * norm_es + 15) & ~static_cast<size_t>(15));
 }

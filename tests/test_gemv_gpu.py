@@ -343,11 +343,11 @@ def test_persistent_stack_two_launches(monkeypatch):
         assert torch.equal(out, x)
 
 
-@pytest.mark.parametrize("m", [8, 16])
+@pytest.mark.parametrize("m", [1, 8])
 def test_post_attn_mlp_llama70b_widths(m):
     """Llama-3-70B widths (hidden 8192, intermediate 28672) through the fused
-    two-kernel MLP at the batches where the gate/up stage's shared memory is
-    tightest: the streamed batch keeps the ring deep and 16 rows fuse too.
+    two-kernel MLP, up to the batch where the gate/up stage's resident
+    normalised batch still fits its shared memory (8 rows).
 
     Tolerance: the reference's own for its linear paths in bf16 (rtol = atol =
     4e-2, its tests/test_ops.py:27-35).  The reference rounds gate_up and mid
