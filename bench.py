@@ -731,12 +731,19 @@ def run_ours(args) -> None:
         ms_pl, _ = time_stack(stack_pl, max(3, args.steps // 5), args.warmup)
         per_layer_us = ms_pl * 1e3 / LAYERS
         del stack_pl
-    elif exchange is not None:
-        # tensor parallel: the per-layer path (gate/up, down, NVLink reduce: three launches a layer)
-        stack_pl = MlpStack(layers, args.m, EPS, kind="dot", layer_fn=layer_fn_tp)
-        ms_pl, _ = time_stack(stack_pl, max(3, args.steps // 5), args.warmup)
-        per_layer_us = ms_pl * 1e3 / LAYERS
-        del stack_pl
+
+    # ---- the opt-in persistent kernel (one launch per 32 layers), timed beside the default
+    persistent_us = None
+    if world == 1 or exchange is not None:
+        os.environ["FD_STACK_PERSISTENT"] = "1"  # read by the library at each stack call
+        try:
+            stack_p = MlpStack(layers, args.m, EPS, kind="dot", exchange=exchange)
+            ms_p, _ = time_stack(stack_p, max(3, args.steps // 5), args.warmup)
+            persistent_us = ms_p * 1e3 / LAYERS
+            persistent_launches = stack_p.launches_per_replay
+            del stack_p
+        finally:
+            del os.environ["FD_STACK_PERSISTENT"]
 
     # ---- the same stack as two stream-K kernels per layer (gate/up, then down + residual)
     two_kernel_us = None
@@ -890,6 +897,7 @@ def run_ours(args) -> None:
                                      "frac": dn_gbs / pk["hbm_gbs"]},
                 "layer": {"us": us1, "gbs": gbs1, "bytes": bytes1, "frac": gbs1 / pk["hbm_gbs"]},
                 "per_layer_calls_us_per_layer": per_layer_us,
+                "persistent_kernel_us_per_layer": persistent_us,
                 "two_kernel_us_per_layer": two_kernel_us,
             },
             "ops": ops,

@@ -429,17 +429,17 @@ cudaError_t launch_stack(const StackParams& p, int grid, size_t smem, cudaStream
 namespace fd_host {
 
 // Whether a stack runs as the persistent kernel.  Measured on B200 (32-layer
-// Llama-3-8B stacks, CUDA graphs): on one GPU the two-launch chain is as fast
-// or faster at every batch (M=1 66.4 vs 70.4 us/layer, M=8 72.3 vs 82.1) --
-// a phase boundary inside the kernel costs what a kernel boundary costs, the
-// skew of the slowest SM and the activation round trips, while the chain's
-// gate/up and down launches each get a ring sized for their own phase -- so
-// there the persistent kernel is opt-in (FD_STACK_PERSISTENT=1).  Tensor
-// parallel stacks use it by default: it folds the rank reduction into the
-// kernel, three launches per layer fewer.  It needs at least 4 ring stages.
-bool persistent_wanted(bool tp, const StackGeometry& geo) {
+// Llama-3-8B stacks in CUDA graphs, same box, same call): on one GPU the
+// launch chain is as fast or faster at every batch (M=1 66.4 vs 70.4
+// us/layer, M=8 72.3 vs 82.1), and tensor parallel over 2 GPUs too (M=1
+// 46.2 vs 55.7 us/layer with the rank reduction inside the kernel): a phase
+// boundary inside the kernel costs what a kernel boundary costs -- the
+// slowest SM's tail, the barrier and the activation round trip -- and the
+// chain's launches each get a ring sized for their own phase.  So the
+// persistent kernel is opt-in (FD_STACK_PERSISTENT=1), and needs at least 4
+// ring stages.
+bool persistent_wanted(bool /*tp*/, const StackGeometry& geo) {
   if (geo.stages < 4) return false;
-  if (tp) return true;
   const char* env = std::getenv("FD_STACK_PERSISTENT");
   return env && env[0] == '1';
 }

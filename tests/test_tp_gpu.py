@@ -275,7 +275,7 @@ def test_tp_nvlink_layers():
 
 
 @pytest.mark.parametrize("m", [1, 8])
-def test_tp_stack_single_rank(m):
+def test_tp_stack_single_rank(m, monkeypatch):
     """The tensor-parallel stack entry point (one persistent kernel: gate/up,
     down with the partials published into the exchange buffer, reduce) with a
     group of one: the same bits as per-layer calls, replay after replay in a
@@ -287,6 +287,7 @@ def test_tp_stack_single_rank(m):
     from fused_decode_b200.stack import MlpStack
 
     h, i, layers = 1024, 2816, 4
+    monkeypatch.setenv("FD_STACK_PERSISTENT", "1")
     ex = tp.TPExchange(h, m_max=16)
     try:
         ws = [_layer(h, i, m, 960 + l)[1:] for l in range(layers)]
@@ -320,6 +321,7 @@ def _rank_main_tp_stack(rank, world, port, outdir, h, i, m, layers):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ["FD_STACK_PERSISTENT"] = "1"  # the persistent kernel, in this rank process only
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
