@@ -740,7 +740,6 @@ def run_ours(args) -> None:
             stack_p = MlpStack(layers, args.m, EPS, kind="dot", exchange=exchange)
             ms_p, _ = time_stack(stack_p, max(3, args.steps // 5), args.warmup)
             persistent_us = ms_p * 1e3 / LAYERS
-            persistent_launches = stack_p.launches_per_replay
             del stack_p
         finally:
             del os.environ["FD_STACK_PERSISTENT"]

@@ -6,7 +6,9 @@
 // griddepcontrol.wait, so it overlaps the previous kernel's tail.
 #include "fd_stream.cuh"
 
+#include <map>
 #include <mutex>
+#include <tuple>
 
 using namespace fd;
 using namespace fd_stream;
@@ -88,6 +90,104 @@ __global__ void __launch_bounds__(MAXT, MINB)
   if (MODE == MODE_GATEUP) norm_to_smem<T>(a, a.hidden, r, s_sumsq, nw_smem, &s_nw_bar);
   grid_dep_launch();
   consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort, ms);
+}
+
+// ------------------------------------------------------------ cluster split
+// LINEAR GEMV for shapes whose 128-row blocks number about the SMs / S
+// (the MLP's down projection: 32 blocks): a thread-block cluster of S = 2 or
+// 4 CTAs takes one block, CTA r streaming K steps [r*ks/S, (r+1)*ks/S) of
+// it.  Every CTA moves the same bytes, no block is shared across clusters,
+// and the split-K sum goes through distributed shared memory: each CTA
+// stores its partial into the cluster leader's shared memory, one cluster
+// barrier, and the leader adds the S partials in rank order (deterministic)
+// and runs the epilogue -- no global slots, fences, counters or atomics.
+// Only the local GPU's shared memory is touched; nothing uses TMA multicast.
+constexpr int kClusterProducers = 2;
+constexpr int kClusterThreads = CONSUMERS + 32 * kClusterProducers;
+constexpr int kClusterMaxSplit = 4;
+
+__host__ __device__ inline size_t cluster_part_bytes(int split) {
+  return static_cast<size_t>(split) * BR * MT_MAX * sizeof(float);
+}
+
+template <typename T, int NT, int KIND, int MP>
+__global__ void __launch_bounds__(kClusterThreads, 1)
+    gemv_cluster_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                        const GemvArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ int s_last, s_abort;
+  __shared__ __align__(8) uint64_t s_mid[2];
+  __shared__ int s_mid_last, s_fast, s_decided;
+  const int64_t xb = static_cast<int64_t>(a.stages) * a.boxes * a.x_slot;
+  const Ring r = carve_ring(smem_raw, a.stages, a.boxes, a.x_slot, xb + cluster_part_bytes(a.cl_split));
+  float* part = reinterpret_cast<float*>(r.xreg + xb);  // [split][BR][MT_MAX]: filled in the leader
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const uint32_t rank = cluster_ctarank();
+  const int split = a.cl_split;
+  const int64_t blk = blockIdx.x / split;
+  const int64_t s0 = blk * a.ks + rank * a.ks / split, s1 = blk * a.ks + (rank + 1) * a.ks / split;
+  const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided, 0u, 1};  // no mid blocks here
+  if (threadIdx.x == 0) {
+    ring_init(r);
+    s_abort = 0;
+  }
+  __syncthreads();
+  cluster_arrive_relaxed();  // phase 1: this CTA (and its shared memory) is running
+
+  Acc<NT> acc;
+  acc.zero();
+  if (warp >= GW) {
+    const int p = warp - GW;
+    if (lane == 0) {
+      prefetch_map(&wmap);
+      prefetch_map(&xmap);
+      produce_phase<MODE_LINEAR>(r, &wmap, &xmap, a, s0, s1, 0, p, kClusterProducers, evict_first_policy(), &s_abort,
+                                 [] {
+                                   grid_dep_wait();  // the activation is the previous kernel's output
+                                   return true;
+                                 });
+      producer_drain(r, s1 - s0, p, kClusterProducers);
+    }
+    __syncwarp();
+    grid_dep_launch();
+  } else {
+    grid_dep_wait();
+    grid_dep_launch();
+    consume_phase<T, NT, KIND, MP, MODE_LINEAR>(a, r, s0, s1, 0, 1, 0, &s_last, &s_abort, ms, &acc);
+  }
+  cluster_wait();  // phase 1 complete: every CTA of the cluster is running
+  if (warp < GW) {
+    float* mine = part + rank * (BR * MT_MAX);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * warp + g + 8 * h, col = 8 * t + 2 * q;
+        st_cluster_f2(cluster_map(mine + row * MT_MAX + col, 0), acc.v[t][2 * h], acc.v[t][2 * h + 1]);
+      }
+  }
+  cluster_arrive();  // phase 2: the partials are in the leader
+  cluster_wait();
+  if (rank == 0 && warp < GW) {
+    Acc<NT> sum;
+    sum.zero();
+    for (int k = 0; k < split; ++k) {
+      const float* pk = part + k * (BR * MT_MAX);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = 16 * warp + g + 8 * h, col = 8 * t + 2 * q;
+          const float2 v = *reinterpret_cast<const float2*>(pk + row * MT_MAX + col);
+          sum.v[t][2 * h] += v.x;
+          sum.v[t][2 * h + 1] += v.y;
+        }
+    }
+    Acc<NT> ex;
+    Epilogue<T, NT, MODE_LINEAR>::extras(a, blk, ex);
+    Epilogue<T, NT, MODE_LINEAR>::run(a, blk, sum, ex, r.xchg);
+  }
 }
 
 // ------------------------------------------------------------ generic GEMV
@@ -177,6 +277,83 @@ cudaError_t dispatch_tma(const CUtensorMap& wm, const CUtensorMap& xm, const Gem
   return L(gemv_tma_kernel<T, 2, 1, 16, MODE, MT1, 1>);
 }
 
+// Cluster size for a LINEAR launch, 0 for stream-K: the largest S in {4, 2}
+// with blocks * S between 80 % and 100 % of the SMs and at least S steps per
+// block; FD_GEMV_CLUSTER=0 turns the cluster split off (tuning).
+int cluster_split(const GemvArgs& a, const Geometry& geo) {
+  const char* env = std::getenv("FD_GEMV_CLUSTER");
+  if (env && env[0] == '0') return 0;
+  const int64_t sms = fd_host::sm_count();
+  const size_t limit = kSmemPerCta;
+  for (int s = kClusterMaxSplit; s >= 2; s /= 2) {
+    const int64_t ctas = a.nblocks * s;
+    if (ctas <= sms && ctas * 10 >= sms * 8 && a.ks >= s &&
+        ring_smem_bytes(linear_x_bytes(a.m, geo.stages, geo.boxes) + cluster_part_bytes(s), geo.stages,
+                        geo.boxes) <= limit)
+      return s;
+  }
+  return 0;
+}
+
+template <typename Kern>
+cudaError_t launch_cluster(Kern kern, const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, size_t smem,
+                           cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.nblocks * a.cl_split));
+  cfg.blockDim = dim3(kClusterThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(a.cl_split);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  // every cluster must be resident at once for the split to pay: else stream-K
+  // (the answer depends on the kernel, its shared memory and the cluster size)
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, size_t, int, int>, int> fits;
+  int dev = 0;
+  (void)cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kern), smem, a.cl_split, dev);
+  int clusters = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = fits.find(key);
+    if (it != fits.end()) clusters = it->second;
+  }
+  if (clusters < 0) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      clusters = 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    fits[key] = clusters;
+  }
+  if (clusters < a.nblocks) return cudaErrorUnsupportedLimit;
+  return cudaLaunchKernelEx(&cfg, kern, wm, xm, a);
+}
+
+template <typename T>
+cudaError_t dispatch_cluster(const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, int kind, size_t smem,
+                             cudaStream_t st) {
+  auto L = [&](auto kern) { return launch_cluster(kern, wm, xm, a, smem, st); };
+  if (kind == FD_KIND_DOT) {
+    if (a.m <= 8) return L(gemv_cluster_kernel<T, 1, 0, 1>);
+    return L(gemv_cluster_kernel<T, 2, 0, 1>);
+  }
+  if (a.m <= 1) return L(gemv_cluster_kernel<T, 1, 1, 1>);
+  if (a.m <= 2) return L(gemv_cluster_kernel<T, 1, 1, 2>);
+  if (a.m <= 4) return L(gemv_cluster_kernel<T, 1, 1, 4>);
+  if (a.m <= 8) return L(gemv_cluster_kernel<T, 1, 1, 8>);
+  return L(gemv_cluster_kernel<T, 2, 1, 16>);
+}
+
 // Launch the stream-K TMA GEMV in LINEAR mode: y = x @ w^T (+bias)(+row_add).
 int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvArgs a, int dtype, int kind,
                   const Workspace& ws, cudaStream_t st) {
@@ -196,6 +373,18 @@ int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvAr
   const int64_t xstride = a.m == 1 ? ((a.k + 7) / 8) * 8 : sxm;
   if (!make_map_2d(&wm, w, a.n, a.k, swn, BR) || !make_map_2d(&xm, x, a.m, a.k, xstride, a.m))
     return FD_ERR_LAUNCH;
+  const int split = cluster_split(a, geo);
+  if (split > 1) {
+    a.cl_split = split;
+    const size_t csmem =
+        ring_smem_bytes(linear_x_bytes(a.m, a.stages, a.boxes) + cluster_part_bytes(split), a.stages, a.boxes);
+    cudaError_t e = dtype == FD_BF16 ? dispatch_cluster<__nv_bfloat16>(wm, xm, a, kind, csmem, st)
+                                     : dispatch_cluster<__half>(wm, xm, a, kind, csmem, st);
+    if (e == cudaSuccess) return FD_OK;
+    if (e != cudaErrorUnsupportedLimit) return FD_ERR_LAUNCH;
+    (void)cudaGetLastError();  // the clusters do not fit the device: stream-K below
+    a.cl_split = 0;
+  }
   const size_t smem = ring_smem_bytes(linear_x_bytes(a.m, a.stages, a.boxes), a.stages, a.boxes);
   cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st)
                                    : dispatch_tma<__half, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st);

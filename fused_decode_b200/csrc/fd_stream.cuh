@@ -104,6 +104,9 @@ struct GemvArgs {
   int32_t tp_rank, tp_world, tp_mmax;
   int64_t tp_data_off;
   const int* tp_seq;  // this rank's round number
+  // cluster split (gemv_cluster_kernel): each block's K steps are divided
+  // among cl_split CTAs of one thread-block cluster
+  int32_t cl_split;
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -214,6 +217,27 @@ FD_DEV void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 FD_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS) : "memory"); }
+
+// ---- thread-block clusters (the CTAs of one cluster share distributed shared memory)
+FD_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of this CTA's shared-memory location `p` in cluster CTA `rank`.
+FD_DEV uint32_t cluster_map(const void* p, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_addr(p)), "r"(rank));
+  return ra;
+}
+FD_DEV void st_cluster_f2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+// Every thread of every CTA of the cluster takes part in each arrive / wait
+// pair (the hardware barrier counts threads, so no thread may skip one).
+FD_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+FD_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+FD_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // Byte offset of 16-byte chunk c of row r inside a 128B-swizzled tile whose
 // rows are 128 bytes (TMA CU_TENSOR_MAP_SWIZZLE_128B, 1024-byte aligned base).
@@ -870,9 +894,12 @@ FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, floa
 
 // Consumer warps' share of one phase: phase steps [s0, s1) at ring indices
 // base ..; flushes every finished block.  Returns false when a wait expired.
+// cl_out: the cluster split (gemv_cluster_kernel) -- the range lies inside
+// one block and its partial is returned here for the cluster's reduction
+// instead of going through the split-K slots.
 template <typename T, int NT, int KIND, int MP, int MODE>
 FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t s1, int64_t base, int64_t G,
-                          int64_t c, int* s_last, int* s_abort, const MidSync& ms) {
+                          int64_t c, int* s_last, int* s_abort, const MidSync& ms, Acc<NT>* cl_out = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int B = r.B;
@@ -1007,7 +1034,9 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
           }
       }
       const bool covered = (s0 <= cb * a.ks) && (s1 >= (cb + 1) * a.ks);
-      if (covered) {
+      if (cl_out) {
+        *cl_out = acc;  // the range's one flush: the cluster reduces it
+      } else if (covered) {
         Acc<NT> ex;
         Epilogue<T, NT, MODE>::extras(a, cb, ex);
         Epilogue<T, NT, MODE>::run(a, cb, acc, ex, r.xchg);

@@ -297,12 +297,14 @@ def test_zz_no_pipeline_timeouts_after_stacks():
 @pytest.mark.parametrize("m", [1, 8])
 def test_persistent_stack_llama8b(m, monkeypatch):
     """The persistent one-kernel stack at Llama-3-8B widths (4 layers): the
-    same bits as one post_attn_mlp call per layer (two launches each), each of
+    same bits as one post_attn_mlp call per layer (two launches each, the
+    down projection split stream-K as the stack splits it), each of
     which matches the oracle on its own input at atol = rtol = 1e-2; captured
     in a CUDA graph it replays the same bits."""
     from fused_decode_b200.stack import MlpStack
 
     monkeypatch.setenv("FD_STACK_PERSISTENT", "1")
+    monkeypatch.setenv("FD_GEMV_CLUSTER", "0")  # the chain's down projection split as the stack splits it
     h, i, layers = 4096, 14336, 4
     dtype = torch.bfloat16
     ws = [_mlp_weights(h, i, dtype, 600 + l) for l in range(layers)]
@@ -328,6 +330,7 @@ def test_persistent_stack_two_launches(monkeypatch):
     """33 layers take two persistent launches (32 + 1): the hand-over between
     them, and the barrier counter left at zero by the first, give the chain's bits."""
     monkeypatch.setenv("FD_STACK_PERSISTENT", "1")
+    monkeypatch.setenv("FD_GEMV_CLUSTER", "0")
     h, i, layers, m = 256, 512, 33, 2
     dtype = torch.bfloat16
     ws = [_mlp_weights(h, i, dtype, 700 + l) for l in range(layers)]
@@ -368,3 +371,37 @@ def test_post_attn_mlp_llama70b_widths(m):
         mid = torch.empty(m, i, device="cuda", dtype=dtype)
         K.mlp_gate_up_out(x, nw, wgu, mid, 1e-5, kind)
         _close(y, O.linear(_np(mid), _np(wd), row_add=_np(x), dtype="bfloat16"))
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+@pytest.mark.parametrize("n,k", [(4096, 14336), (4096, 4096), (8192, 28672), (4096, 1792)])
+def test_linear_cluster_split(n, k, m):
+    """The cluster-split GEMV (blocks shared by a 2- or 4-CTA cluster, partials
+    summed through distributed shared memory) against the oracle, with bias
+    and row_add, run after run the same bits; and against the stream-K split
+    within the parity bar."""
+    import os
+
+    dtype = torch.bfloat16
+    g = _gen(900 + m)
+    x = torch.randn(m, k, device="cuda", dtype=dtype, generator=g)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(dtype)
+    b = (torch.randn(n, device="cuda", generator=g) * 0.02).to(dtype)
+    ra = torch.randn(m, n, device="cuda", dtype=dtype, generator=g)
+    ref = O.linear(_np(x), _np(w), _np(b), _np(ra), "bfloat16")
+    outs = []
+    for _ in range(2):
+        y = torch.empty(m, n, device="cuda", dtype=dtype)
+        K.linear_out(x, w, y, bias=b, row_add=ra, kind="dot")
+        outs.append(y)
+    _close(outs[0], ref)
+    assert torch.equal(outs[0], outs[1])
+    os.environ["FD_GEMV_CLUSTER"] = "0"
+    try:
+        y_sk = torch.empty(m, n, device="cuda", dtype=dtype)
+        K.linear_out(x, w, y_sk, bias=b, row_add=ra, kind="dot")
+    finally:
+        del os.environ["FD_GEMV_CLUSTER"]
+    _close(y_sk, ref)
+    torch.cuda.synchronize()
+    assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()

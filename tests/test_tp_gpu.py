@@ -288,6 +288,7 @@ def test_tp_stack_single_rank(m, monkeypatch):
 
     h, i, layers = 1024, 2816, 4
     monkeypatch.setenv("FD_STACK_PERSISTENT", "1")
+    monkeypatch.setenv("FD_GEMV_CLUSTER", "0")
     ex = tp.TPExchange(h, m_max=16)
     try:
         ws = [_layer(h, i, m, 960 + l)[1:] for l in range(layers)]
@@ -322,6 +323,7 @@ def _rank_main_tp_stack(rank, world, port, outdir, h, i, m, layers):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["FD_STACK_PERSISTENT"] = "1"  # the persistent kernel, in this rank process only
+    os.environ["FD_GEMV_CLUSTER"] = "0"  # and the per-layer path split stream-K as the kernel splits it
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
