@@ -710,186 +710,208 @@ FD_DEV void producer_drain(const Ring& r, int64_t end, int p, int P) {
 // RMSNorm of the m hidden rows into the GATEUP X region, rounded to T
 // (reference.py:389 rounds `normed` to the activation dtype), stored as
 // 64-column chunks of [m x 128 B] with the same swizzle as a TMA tile;
-// columns past k (to the end of the last step) are zero.  The hidden rows are
-// read through L2 (they may have been written earlier in this kernel).  Under
-// full HBM load an L2 round trip costs microseconds, so rows are processed in
-// groups whose loads (hidden and norm weight) are all issued at once: one
-// round trip per group -- a single group for m * k <= 8 * 256 * 8 (k <= 8192
-// here; wider rows take two passes).
-// norm_to_smem is called by all consumer threads and ends with a consumer
-// barrier.  The norm weight (k elements of norm_dtype) is in shared memory at
-// `nw`, copied there by a bulk TMA load at kernel start that completes on `nw_bar`.
-FD_DEV void load8_smem_as_f32(const unsigned char* p, int dtype, float* f) {
-  if (dtype == FD_F32) {
-    const float4 lo = *reinterpret_cast<const float4*>(p), hi = *reinterpret_cast<const float4*>(p + 16);
-    f[0] = lo.x; f[1] = lo.y; f[2] = lo.z; f[3] = lo.w;
-    f[4] = hi.x; f[5] = hi.y; f[6] = hi.z; f[7] = hi.w;
-  } else if (dtype == FD_BF16) {
-    unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(p), f);
-  } else {
-    unpack8<__half>(*reinterpret_cast<const uint4*>(p), f);
-  }
+// columns past k (to the end of the last step) are zero.  The norm weight
+// (k elements of norm_dtype) is in shared memory at `nw`, copied there by a
+// bulk TMA load that completes on `nw_bar`.  Called by all consumer threads;
+// ends with a consumer barrier.
+//
+// Every CTA normalises the whole batch between the launch (or the phase
+// barrier) and its first tensor-core step, so this latency- and issue-bound
+// SIMT work sits on the critical path (measured alone on one B200 SM at
+// k = 4096: about 1,800 cycles at m = 1 and 5,700 at m = 8).  The steps:
+//   1. cp.async (through L2: rows written earlier in the same kernel are
+//      read coherently) of every 16-byte vector of every row straight to its
+//      final place in X -- one round trip for the whole batch;
+//   2. each thread's sums of squares over the vectors it copied (readable by
+//      that thread after its own wait), RB rows at a time so that their
+//      shared loads, FMAs and warp butterflies overlap;
+//   3. one thread per row adds the warps' sums (in warp order) and stores
+//      the row's scale rsqrt(mean + eps) -- all rows at once;
+//   4. the scale in place, RB rows per norm-weight vector (loaded once):
+//      (x * scale) * w, rounded to T.
+// The fp32 products go through packed f32x2 multiplies (sm_100): each lane
+// rounds like the scalar multiply, so the bits are those of x * scale * w.
+// Sum order is fixed (even and odd columns of a thread's vectors as two
+// running FMA sums, then lanes by butterfly, then warps in index order), so
+// results are run-to-run exact.
+FD_DEV uint64_t f32x2_of(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
 }
-
-// JV: 16-byte vectors per thread per row (compile-time, so the row / vector
-// split of the register batch folds away; 0 = rows too wide for one batch).
-// REGS: 16-byte vectors of hidden held per thread per group of rows.
-// NR: the exact row count when it is known at compile time (0: m at run time).
-template <typename T, int JV, int REGS = 8, int NR = 0>
-FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
-                      const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity);
-
-// `hidden`: the rows to normalise (a.hidden for a single launch; the stack
-// passes each layer's input).
+FD_DEV float2 f32x2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+FD_DEV uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+FD_DEV uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// one 32-bit word of two T elements -> {lo, hi} as f32x2 (exact)
 template <typename T>
-FD_DEV void norm_to_smem(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
-                         const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity = 0) {
-  const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
-  const int jv = (nvec_pad + CONSUMERS - 1) / CONSUMERS;
-  // The prologue runs right after the launch, so its unrolled code is on the
-  // critical path.  The smallest batches get a register group of exactly the
-  // vectors they use (row count fixed at compile time: no guarded, predicated
-  // slots); that measured 1.1 us/layer faster at m = 1 than 8-vector groups.
-  // Other batches that fit four vectors per thread take the 4-vector group;
-  // wider ones keep 8 vectors, so fewer groups (fewer load round trips).
-  if (jv == 2 && a.m == 1) {
-    norm_rows<T, 2, 2, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
-    return;
-  }
-  if (jv == 2 && a.m == 2) {
-    norm_rows<T, 2, 4, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
-    return;
-  }
-  if (jv == 1 && a.m == 1) {
-    norm_rows<T, 1, 1, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
-    return;
-  }
-  if (jv == 1 && a.m <= 4) {
-    norm_rows<T, 1, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
-    return;
-  }
-  switch (jv) {
-    case 1: norm_rows<T, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
-    case 2: norm_rows<T, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
-    case 3: norm_rows<T, 3>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
-    case 4: norm_rows<T, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
-    default: norm_rows<T, 0>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity); break;
+FD_DEV uint64_t pair_f32x2(uint32_t w) {
+  const float2 f = unpack2<T>(w);
+  return f32x2_of(f.x, f.y);
+}
+// 8 norm-weight elements of a runtime dtype at p (shared memory) as 4 f32x2 pairs
+FD_DEV void nw_pairs(const unsigned char* p, int dtype, uint64_t* w) {
+  if (dtype == FD_F32) {
+    const uint4 lo = *reinterpret_cast<const uint4*>(p), hi = *reinterpret_cast<const uint4*>(p + 16);
+    w[0] = (static_cast<uint64_t>(lo.y) << 32) | lo.x;
+    w[1] = (static_cast<uint64_t>(lo.w) << 32) | lo.z;
+    w[2] = (static_cast<uint64_t>(hi.y) << 32) | hi.x;
+    w[3] = (static_cast<uint64_t>(hi.w) << 32) | hi.z;
+  } else {
+    const uint4 r = *reinterpret_cast<const uint4*>(p);
+    if (dtype == FD_BF16) {
+      w[0] = pair_f32x2<__nv_bfloat16>(r.x); w[1] = pair_f32x2<__nv_bfloat16>(r.y);
+      w[2] = pair_f32x2<__nv_bfloat16>(r.z); w[3] = pair_f32x2<__nv_bfloat16>(r.w);
+    } else {
+      w[0] = pair_f32x2<__half>(r.x); w[1] = pair_f32x2<__half>(r.y);
+      w[2] = pair_f32x2<__half>(r.z); w[3] = pair_f32x2<__half>(r.w);
+    }
   }
 }
+FD_DEV uint4 ld_shared16(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_addr(p))
+               : "memory");
+  return v;
+}
+FD_DEV void cp_async16_cg(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+FD_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <typename T, int JV, int REGS, int NR>
+// byte offset of row mrow's 16-byte vector v in the GATEUP X region of m rows
+FD_DEV int gateup_x_off(int m, int mrow, int v) { return ((v >> 3) * m + mrow) * 128 + (((v & 7) ^ (mrow & 7)) << 4); }
+
+template <typename T, int RB>
 FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
                       const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  unsigned char* xs = r.xreg;
+  const int m = a.m;
   const int nvec = static_cast<int>(a.k / 8);
   const int nvec_pad = static_cast<int>(a.ks * r.B * (KC / 8));
-  constexpr int jv = JV;
-  const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
-  if constexpr (JV > 0) {
-    constexpr int rows_per_group = REGS / JV;
-    for (int r0 = 0; r0 < a.m; r0 += rows_per_group) {
-      const int nr = NR > 0 ? NR : min(rows_per_group, a.m - r0);
-      uint4 hv[REGS];
-      // issue every load of the group first
-#pragma unroll
-      for (int e = 0; e < REGS; ++e) {
-        const int rr = e / jv, j = e - (e / jv) * jv;
-        const int v = tid + j * CONSUMERS;
-        hv[e] = make_uint4(0, 0, 0, 0);
-        if (rr < nr && v < nvec)
-          hv[e] = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(hidden) +
-                                                         (r0 + rr) * a.hidden_stride) + v);
-      }
-      float ss[REGS];
-#pragma unroll
-      for (int e = 0; e < REGS; ++e) {
-        float f[8];
-        unpack8<T>(hv[e], f);
-        float t = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) t += f[q] * f[q];
-        ss[e] = t;
-      }
-      // per-row partial sums -> warp -> shared
-#pragma unroll
-      for (int rr = 0; rr < REGS; ++rr) {
-        if (rr < nr) {
-          float t = 0.f;
-#pragma unroll
-          for (int e = 0; e < REGS; ++e)
-            if (e / jv == rr) t += ss[e];
-          t = warp_sum(t);
-          if (lane == 0) s_sumsq[warp][rr] = t;
-        }
-      }
-      consumer_sync();
-      if (r0 == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
-      // one scale per row of the group, then a short loop over the vectors
-      float inv[rows_per_group];
-#pragma unroll
-      for (int rr = 0; rr < rows_per_group; ++rr) {
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < GW; ++w) tot += s_sumsq[w][rr];
-        inv[rr] = rr < nr ? rsqrtf(tot / static_cast<float>(a.k) + a.eps) : 0.f;  // rows past m: unused
-      }
-#pragma unroll
-      for (int e = 0; e < REGS; ++e) {
-        const int rr = e / jv, j = e - (e / jv) * jv;
-        const int v = tid + j * CONSUMERS;
-        if (rr < nr && v < nvec_pad) {
-          uint4 packed = make_uint4(0, 0, 0, 0);
-          if (v < nvec) {
-            float f[8], w[8], o[8];
-            unpack8<T>(hv[e], f);
-            load8_smem_as_f32(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, w);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) o[q] = f[q] * inv[rr] * w[q];
-            packed = pack8<T>(o);
-          }
-          const int mrow = r0 + rr, chunk = v >> 3, cc = v & 7;
-          st_shared16(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4), packed);
-        }
-      }
-      consumer_sync();  // s_sumsq is reused by the next group
+  unsigned char* xs = r.xreg;
+  const T* hb = reinterpret_cast<const T*>(hidden);
+  // 1. every vector of every row to its place in X (zeros past k)
+#pragma unroll 1
+  for (int v = tid; v < nvec_pad; v += CONSUMERS) {
+    if (v < nvec) {
+#pragma unroll 4
+      for (int mrow = 0; mrow < m; ++mrow)
+        cp_async16_cg(xs + gateup_x_off(m, mrow, v), reinterpret_cast<const uint4*>(hb + mrow * a.hidden_stride) + v);
+    } else {
+      for (int mrow = 0; mrow < m; ++mrow) st_shared16(xs + gateup_x_off(m, mrow, v), make_uint4(0, 0, 0, 0));
     }
-    return;
-  } else {
-  // Very wide rows: two passes per row, loads of a pass in flight together.
-  for (int mrow = 0; mrow < a.m; ++mrow) {
-    const uint4* hr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(hidden) + mrow * a.hidden_stride);
-    float ss = 0.f;
+  }
+  cp_async_wait_all();
+  // 2. sums of squares, RB rows at a time
+#pragma unroll 1
+  for (int r0 = 0; r0 < m; r0 += RB) {
+    uint64_t acc[RB];
+#pragma unroll
+    for (int q = 0; q < RB; ++q) acc[q] = 0;  // {+0.f, +0.f}
+#pragma unroll 1
     for (int v = tid; v < nvec; v += CONSUMERS) {
-      float f[8];
-      unpack8<T>(__ldcg(hr + v), f);
+      uint4 raw[RB];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) ss += f[q] * f[q];
+      for (int q = 0; q < RB; ++q)
+        if (RB == 1 || r0 + q < m) raw[q] = ld_shared16(xs + gateup_x_off(m, r0 + q, v));
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+        if (RB == 1 || r0 + q < m) {
+          const uint64_t p0 = pair_f32x2<T>(raw[q].x), p1 = pair_f32x2<T>(raw[q].y);
+          const uint64_t p2 = pair_f32x2<T>(raw[q].z), p3 = pair_f32x2<T>(raw[q].w);
+          acc[q] = fma_f32x2(p0, p0, acc[q]);
+          acc[q] = fma_f32x2(p1, p1, acc[q]);
+          acc[q] = fma_f32x2(p2, p2, acc[q]);
+          acc[q] = fma_f32x2(p3, p3, acc[q]);
+        }
+      }
     }
-    ss = warp_sum(ss);
-    if (lane == 0) s_sumsq[warp][0] = ss;
-    consumer_sync();
+    float t[RB];
+#pragma unroll
+    for (int q = 0; q < RB; ++q) {
+      const float2 h = f32x2_split(acc[q]);
+      t[q] = h.x + h.y;
+    }
+#pragma unroll
+    for (int q = 0; q < RB; ++q) t[q] = warp_sum(t[q]);
+    if (lane == 0) {
+#pragma unroll
+      for (int q = 0; q < RB; ++q)
+        if (RB == 1 || r0 + q < m) s_sumsq[warp][r0 + q] = t[q];
+    }
+  }
+  consumer_sync();
+  // 3. the rows' scales (row i by thread i; it alone reads column i)
+  if (tid < m) {
     float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < GW; ++w) tot += s_sumsq[w][0];
-    const float inv = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
-    if (mrow == 0 && !mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
-    for (int v = tid; v < nvec_pad; v += CONSUMERS) {
-      uint4 packed = make_uint4(0, 0, 0, 0);
-      if (v < nvec) {
-        float f[8], wv[8], o[8];
-        unpack8<T>(__ldcg(hr + v), f);
-        load8_smem_as_f32(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, wv);
+    for (int w = 0; w < GW; ++w) tot += s_sumsq[w][tid];
+    s_sumsq[0][tid] = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
+  }
+  if (!mbar_wait(nw_bar, nw_parity)) atomicOr(a.status, kStatusFullTimeout);
+  consumer_sync();
+  // 4. scale in place
+  const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
+#pragma unroll 1
+  for (int v = tid; v < nvec; v += CONSUMERS) {
+    uint64_t w[4];
+    nw_pairs(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, w);
+#pragma unroll 1
+    for (int r0 = 0; r0 < m; r0 += RB) {
+      uint4 raw[RB];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) o[q] = f[q] * inv * wv[q];
-        packed = pack8<T>(o);
+      for (int q = 0; q < RB; ++q)
+        if (RB == 1 || r0 + q < m) raw[q] = ld_shared16(xs + gateup_x_off(m, r0 + q, v));
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+        if (RB == 1 || r0 + q < m) {
+          const float inv = s_sumsq[0][r0 + q];
+          const uint64_t i2 = f32x2_of(inv, inv);
+          const float2 o0 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(raw[q].x), i2), w[0]));
+          const float2 o1 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(raw[q].y), i2), w[1]));
+          const float2 o2 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(raw[q].z), i2), w[2]));
+          const float2 o3 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(raw[q].w), i2), w[3]));
+          uint4 packed;
+          packed.x = pack2<T>(o0.x, o0.y);
+          packed.y = pack2<T>(o1.x, o1.y);
+          packed.z = pack2<T>(o2.x, o2.y);
+          packed.w = pack2<T>(o3.x, o3.y);
+          st_shared16(xs + gateup_x_off(m, r0 + q, v), packed);
+        }
       }
-      const int chunk = v >> 3, cc = v & 7;
-      st_shared16(xs + (static_cast<int64_t>(chunk) * a.m + mrow) * 128 + ((cc ^ (mrow & 7)) << 4), packed);
     }
-    consumer_sync();
   }
-  }
+  consumer_sync();
+}
+
+// `hidden`: the rows to normalise (a.hidden for a single launch; the stack
+// passes each layer's input).  The row block RB is the batch rounded up to
+// 1, 2, 4 or 8 (batches above 8 take two blocks).
+template <typename T>
+FD_DEV void norm_to_smem(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
+                         const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity = 0) {
+  if (a.m == 1)
+    norm_rows<T, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
+  else if (a.m == 2)
+    norm_rows<T, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
+  else if (a.m <= 4)
+    norm_rows<T, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
+  else
+    norm_rows<T, 8>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
 }
 
 // Consumer warps' share of one phase: phase steps [s0, s1) at ring indices
