@@ -97,17 +97,22 @@ __global__ void __launch_bounds__(MAXT, MINB)
 // (the MLP's down projection: 32 blocks): a thread-block cluster of S = 2 or
 // 4 CTAs takes one block, CTA r streaming K steps [r*ks/S, (r+1)*ks/S) of
 // it.  Every CTA moves the same bytes, no block is shared across clusters,
-// and the split-K sum goes through distributed shared memory: each CTA
-// stores its partial into the cluster leader's shared memory, one cluster
-// barrier, and the leader adds the S partials in rank order (deterministic)
-// and runs the epilogue -- no global slots, fences, counters or atomics.
-// Only the local GPU's shared memory is touched; nothing uses TMA multicast.
+// and the split-K sum goes through distributed shared memory: each other
+// CTA sends its partial into the cluster leader's shared memory with
+// st.async, counted in bytes on an mbarrier there, and exits; the leader
+// waits on that mbarrier alone, adds the S partials in rank order
+// (deterministic) and runs the epilogue -- no global slots, fences,
+// counters, atomics or cluster barrier at the end.  Only the local GPU's
+// shared memory is touched; nothing uses TMA multicast.
 constexpr int kClusterProducers = 2;
 constexpr int kClusterThreads = CONSUMERS + 32 * kClusterProducers;
 constexpr int kClusterMaxSplit = 4;
 
+// Partial rows in the leader are padded from MT_MAX to 20 floats: a warp's
+// float2 reads of rows 16w + g (g = 0..7) then touch each bank at most twice.
+constexpr int kPartStride = 20;
 __host__ __device__ inline size_t cluster_part_bytes(int split) {
-  return static_cast<size_t>(split) * BR * MT_MAX * sizeof(float);
+  return static_cast<size_t>(split - 1) * BR * kPartStride * sizeof(float);
 }
 
 template <typename T, int NT, int KIND, int MP>
@@ -117,10 +122,11 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   __shared__ int s_last, s_abort;
   __shared__ __align__(8) uint64_t s_mid[2];
+  __shared__ __align__(8) uint64_t s_part_full;  // leader: the other CTAs' partials have landed
   __shared__ int s_mid_last, s_fast, s_decided;
   const int64_t xb = static_cast<int64_t>(a.stages) * a.boxes * a.x_slot;
   const Ring r = carve_ring(smem_raw, a.stages, a.boxes, a.x_slot, xb + cluster_part_bytes(a.cl_split));
-  float* part = reinterpret_cast<float*>(r.xreg + xb);  // [split][BR][MT_MAX]: filled in the leader
+  float* part = reinterpret_cast<float*>(r.xreg + xb);  // [split - 1][BR][kPartStride]: in the leader
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const uint32_t rank = cluster_ctarank();
@@ -129,14 +135,18 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
   const int64_t s0 = blk * a.ks + rank * a.ks / split, s1 = blk * a.ks + (rank + 1) * a.ks / split;
   const MidSync ms{&s_mid[0], &s_mid[1], &s_mid_last, &s_fast, &s_decided, 0u, 1};  // no mid blocks here
   if (threadIdx.x == 0) {
-    ring_init(r);
+    mbar_init(&s_part_full, 1);
+    ring_init(r);  // ends with the mbarrier-init fence (cluster scope)
     s_abort = 0;
+    // the leader expects 16 * NT bytes from every consumer thread of the other CTAs
+    if (rank == 0) mbar_expect_tx(&s_part_full, static_cast<uint32_t>((split - 1) * CONSUMERS * NT * 16));
   }
   __syncthreads();
   cluster_arrive_relaxed();  // phase 1: this CTA (and its shared memory) is running
 
-  Acc<NT> acc;
+  Acc<NT> acc, ex;
   acc.zero();
+  ex.zero();
   if (warp >= GW) {
     const int p = warp - GW;
     if (lane == 0) {
@@ -153,41 +163,59 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
     grid_dep_launch();
   } else {
     grid_dep_wait();
+    // The leader's epilogue terms (bias, residual rows) are inputs: load them
+    // now, so their L2 round trip overlaps the weight stream instead of
+    // following the partials' arrival at the end.
+    if (rank == 0) Epilogue<T, NT, MODE_LINEAR>::extras(a, blk, ex);
     grid_dep_launch();
+    // Phase 1 complete (every CTA of the cluster is running): waited here,
+    // where the first stage's latency hides it, not after the stream.
+    cluster_wait();
     consume_phase<T, NT, KIND, MP, MODE_LINEAR>(a, r, s0, s1, 0, 1, 0, &s_last, &s_abort, ms, &acc);
   }
-  cluster_wait();  // phase 1 complete: every CTA of the cluster is running
-  if (warp < GW) {
-    float* mine = part + rank * (BR * MT_MAX);
+  if (warp >= GW) {
+    cluster_wait();  // phase 1 (long complete): every thread takes part in each arrive / wait pair
+    return;
+  }
+  if (rank != 0) {
+    // The partial goes to the leader with st.async, counted on its mbarrier:
+    // no fence and no second cluster barrier, and this CTA is done.
+    const uint32_t bar = cluster_map(&s_part_full, 0);
+    float* slot = part + (rank - 1) * (BR * kPartStride);
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int row = 16 * warp + g + 8 * h, col = 8 * t + 2 * q;
-        st_cluster_f2(cluster_map(mine + row * MT_MAX + col, 0), acc.v[t][2 * h], acc.v[t][2 * h + 1]);
+        st_async_f2(cluster_map(slot + row * kPartStride + col, 0), acc.v[t][2 * h], acc.v[t][2 * h + 1], bar);
+      }
+    return;
+  }
+  if (!mbar_wait_cluster(&s_part_full, 0)) {
+    atomicOr(a.status, kStatusFullTimeout);
+    return;
+  }
+  // rank order: 0 + (the leader's own partial, from registers) + rank 1 + ...
+  Acc<NT> sum;
+  sum.zero();
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sum.v[t][e] += acc.v[t][e];
+#pragma unroll 3
+  for (int k = 1; k < split; ++k) {
+    const float* pk = part + (k - 1) * (BR * kPartStride);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * warp + g + 8 * h, col = 8 * t + 2 * q;
+        const float2 v = *reinterpret_cast<const float2*>(pk + row * kPartStride + col);
+        sum.v[t][2 * h] += v.x;
+        sum.v[t][2 * h + 1] += v.y;
       }
   }
-  cluster_arrive();  // phase 2: the partials are in the leader
-  cluster_wait();
-  if (rank == 0 && warp < GW) {
-    Acc<NT> sum;
-    sum.zero();
-    for (int k = 0; k < split; ++k) {
-      const float* pk = part + k * (BR * MT_MAX);
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = 16 * warp + g + 8 * h, col = 8 * t + 2 * q;
-          const float2 v = *reinterpret_cast<const float2*>(pk + row * MT_MAX + col);
-          sum.v[t][2 * h] += v.x;
-          sum.v[t][2 * h + 1] += v.y;
-        }
-    }
-    Acc<NT> ex;
-    Epilogue<T, NT, MODE_LINEAR>::extras(a, blk, ex);
-    Epilogue<T, NT, MODE_LINEAR>::run(a, blk, sum, ex, r.xchg);
-  }
+  Epilogue<T, NT, MODE_LINEAR>::run(a, blk, sum, ex, r.xchg);
 }
 
 // ------------------------------------------------------------ generic GEMV

@@ -160,6 +160,17 @@ FD_DEV uint32_t mbar_try(uint32_t addr, uint32_t parity) {
       : "memory");
   return ok;
 }
+// As mbar_try, with acquire at cluster scope: for data other CTAs of the
+// cluster wrote with st.async against this mbarrier.
+FD_DEV uint32_t mbar_try_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.b32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok;
+}
 // Wait for the phase with the given parity to complete; false after kWaitNs.
 FD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_addr(bar);
@@ -167,6 +178,16 @@ FD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try(addr, parity)) return true;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+// mbar_wait for a barrier completed by other CTAs' st.async (acquire.cluster).
+FD_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  if (mbar_try_cluster(addr, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_cluster(addr, parity)) return true;
     if (globaltimer() - t0 > kWaitNs) return false;
   }
 }
@@ -232,6 +253,14 @@ FD_DEV uint32_t cluster_map(const void* p, uint32_t rank) {
 }
 FD_DEV void st_cluster_f2(uint32_t addr, float a, float b) {
   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+// Asynchronous store of two floats to the shared::cluster address `addr`,
+// counted (8 bytes) on the mbarrier at shared::cluster address `bar` in the
+// same CTA: the receiver learns of the data from the mbarrier alone.
+FD_DEV void st_async_f2(uint32_t addr, float a, float b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(a), "f"(b), "r"(bar)
+               : "memory");
 }
 // Every thread of every CTA of the cluster takes part in each arrive / wait
 // pair (the hardware barrier counts threads, so no thread may skip one).
