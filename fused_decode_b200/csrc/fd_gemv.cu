@@ -56,10 +56,9 @@ __global__ void __launch_bounds__(MAXT, MINB)
     // The split-K counters are shared with the previous launch on this
     // workspace: look at them only once that launch has completed.
     grid_dep_wait();
-    if (lane == 0) {
-      announce_mid(a, ms, s0, s1, G, &s_abort);
-      if (MODE == MODE_GATEUP) watch_final(a, ms, s0, s1, G, c);
-    }
+    if (lane == 0) announce_mid(a, ms, s0, s1, G, &s_abort);
+    __syncwarp();
+    if (MODE == MODE_GATEUP) watch_final_staged<NT>(a, ms, s0, s1, G, c, r.fin);
     grid_dep_launch();
     return;
   }
@@ -444,7 +443,14 @@ int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, c
   a.norm_w = norm_w; a.norm_dtype = norm_dtype; a.eps = eps;
   CUtensorMap gm;
   if (!make_gate_up_map(&gm, w_gate_up, h, i, s_gu)) return FD_ERR_LAUNCH;
-  const size_t smem = ring_smem_bytes(gateup_region_bytes(m, a.ks, a.boxes, h, nes), a.stages, a.boxes);
+  size_t smem = ring_smem_bytes(gateup_region_bytes(m, a.ks, a.boxes, h, nes), a.stages, a.boxes);
+  // room for the final block's staged partials (batches up to 8 rows), where
+  // it costs no ring stage
+  const size_t fin = fin_stage_bytes(1);
+  if (m <= 8 && smem + fin <= kSmemPerCta) {
+    smem += fin;
+    a.fin_stage = 1;
+  }
   cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st)
                                    : dispatch_tma<__half, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st);
   return from_cuda(e);

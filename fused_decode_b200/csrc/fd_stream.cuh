@@ -107,6 +107,9 @@ struct GemvArgs {
   // cluster split (gemv_cluster_kernel): each block's K steps are divided
   // among cl_split CTAs of one thread-block cluster
   int32_t cl_split;
+  // GATEUP stream-K: shared memory after the ring holds the final block's
+  // later contributors' partials, staged by the announcer warp (fin_stage_ok)
+  int32_t fin_stage;
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -527,6 +530,42 @@ FD_DEV void reduce_block(const GemvArgs& a, int64_t blk, float* xchg, int64_t G,
   if (threadIdx.x == 0) a.counters[blk] = 0;
 }
 
+// reduce_block for the head of its final block when every other contributor
+// has published and their partials are staged in shared memory (`fin`): the
+// same sum, in the same order -- 0 + own + each later contributor in CTA
+// order, then + 0 for reduce_block's unused batch entries (x + 0 turns -0
+// into +0, so it stays) -- hence the same bits.
+template <typename T, int NT, int MODE>
+FD_DEV void reduce_staged(const GemvArgs& a, int64_t blk, const float* fin, float* xchg, int64_t G,
+                          const Acc<NT>& ex, const Acc<NT>& own, int64_t c) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int others = static_cast<int>(cta_of((blk + 1) * a.ks - 1, a.total, G) - c);
+  Acc<NT> sum;
+  sum.zero();
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sum.v[t][e] += own.v[t][e];
+  for (int o = 1; o <= others; ++o) {
+    const float* sp = fin + (o - 1) * (BR * 8 * NT);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float2 v = *reinterpret_cast<const float2*>(sp + (16 * warp + g + 8 * h) * 8 * NT + 8 * t + 2 * q);
+        sum.v[t][2 * h] += v.x;
+        sum.v[t][2 * h + 1] += v.y;
+      }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sum.v[t][e] += 0.f;
+  Epilogue<T, NT, MODE>::run(a, blk, sum, ex, xchg);
+  if (threadIdx.x == 0) a.counters[blk] = 0;
+}
+
 // Publish the partial of block blk (already in this CTA's slot) and, if this
 // CTA is the block's last contributor, reduce it.  All consumer threads.
 template <typename T, int NT, int MODE>
@@ -595,6 +634,81 @@ FD_DEV void watch_final(const GemvArgs& a, const MidSync& ms, int64_t s0, int64_
   }
 }
 
+// The final block's later contributors publish at the start of their ranges,
+// long before the head reaches its last step, yet reading their partials
+// from L2 there (behind a fence, with HBM saturated) costs about 2 us at the
+// end of most ranges -- the kernel's critical tail.  So, where the launch
+// reserved the room (GemvArgs::fin_stage), the announcer warp copies them
+// into shared memory as soon as they are published: at most kFinOthers
+// contributors, the 8 * NT columns of each row that the MMA fragments hold.
+constexpr int kFinOthers = 2;
+__host__ __device__ inline size_t fin_stage_bytes(int nt) {
+  return static_cast<size_t>(kFinOthers) * BR * 8 * nt * sizeof(float);
+}
+// Whether the final block of range [s0, s1) of CTA c is served from staged
+// partials.  Batches up to 8 rows (one 8-column MMA tile, NT = 1) only: the
+// 16-row kernels have no registers to spare for the staging code.
+template <int NT>
+FD_DEV bool fin_staged(const GemvArgs& a, int64_t s1, int64_t G, int64_t c) {
+  if (NT != 1 || !a.fin_stage) return false;
+  const int64_t bf = (s1 - 1) / a.ks;
+  return cta_of((bf + 1) * a.ks - 1, a.total, G) - c <= kFinOthers;
+}
+
+// watch_final for the whole announcer warp (lane 0 polls), staging the other
+// contributors' partials into `fin` before raising the flag when fin_staged.
+template <int NT>
+FD_DEV void watch_final_staged(const GemvArgs& a, const MidSync& ms, int64_t s0, int64_t s1, int64_t G, int64_t c,
+                               float* fin) {
+  if (!head_of_final(s0, s1, a.ks)) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t bf = (s1 - 1) / a.ks;
+  const int others = static_cast<int>(cta_of((bf + 1) * a.ks - 1, a.total, G) - c);
+  const uint64_t t0 = globaltimer();
+  int state = 0;  // 1: every other contributor has published; 2: stop watching
+  while (true) {
+    if (lane == 0) {
+      if (*reinterpret_cast<volatile int*>(ms.decided) == ms.tag || globaltimer() - t0 > kWaitNs)
+        state = 2;
+      else if (ld_acquire_gpu(a.counters + bf) == others)
+        state = 1;
+    }
+    state = __shfl_sync(0xffffffffu, state, 0);
+    if (state != 0) break;
+    __nanosleep(1000);  // a light poll: the answer is only needed at the end of the range
+  }
+  if (state == 2) return;
+  __syncwarp();  // lane 0's acquire of the count orders every lane's slot reads after it
+  if (fin_staged<NT>(a, s1, G, c)) {
+    constexpr int V = 2 * NT;             // float4 per row
+    constexpr int PER = BR * V / 32;      // float4 per lane per contributor
+    for (int o = 1; o <= others; ++o) {
+      const int64_t cc = c + o;
+      const int sl = bf != range_start(cc, a.total, G) / a.ks ? 1 : 0;
+      const float* rp = a.slots + (cc * 2 + sl) * (BR * MT_MAX);
+      float* dst = fin + (o - 1) * (BR * 8 * NT);
+      constexpr int CH = 8;  // float4 in flight per lane (registers: the consumers' budget is tight)
+#pragma unroll
+      for (int u0 = 0; u0 < PER; u0 += CH) {
+        float4 v[CH];
+#pragma unroll
+        for (int u = 0; u < CH; ++u) {
+          const int idx = lane + 32 * (u0 + u);
+          v[u] = __ldcg(reinterpret_cast<const float4*>(rp + (idx / V) * MT_MAX) + idx % V);
+        }
+#pragma unroll
+        for (int u = 0; u < CH; ++u) {
+          const int idx = lane + 32 * (u0 + u);
+          reinterpret_cast<float4*>(dst + (idx / V) * 8 * NT)[idx % V] = v[u];
+        }
+      }
+    }
+    __syncwarp();
+    __threadfence_block();  // the staged partials before the flag
+  }
+  if (lane == 0) *reinterpret_cast<volatile int*>(ms.fast) = ms.tag;
+}
+
 FD_DEV bool has_mid_block(int64_t s0, int64_t s1, int64_t ks) { return s0 % ks != 0 && (s0 / ks + 1) * ks < s1; }
 
 // Lane 0 of the announcer warp.
@@ -620,6 +734,7 @@ FD_DEV void announce_mid(const GemvArgs& a, const MidSync& ms, int64_t s0, int64
 // ------------------------------------------------------------ the ring
 // Shared-memory layout (1024-byte aligned base):
 //   [W ring: S x B x 16 KB][X region][xchg: 64 x 16 floats][full[12]][empty[12]]
+//   [fin: GATEUP launches with fin_stage, kFinOthers x BR x 8 * NT floats]
 // X region: LINEAR activation boxes (S x B x x_slot), or the GATEUP normalised
 // batch (ks x B chunks of [m x 128 B]).
 struct Ring {
@@ -628,6 +743,7 @@ struct Ring {
   float* xchg;
   uint64_t* full;
   uint64_t* empty;
+  float* fin;  // GATEUP with fin_stage: [kFinOthers][BR][8 * NT] staged partials
   int S, B, x_slot;
   int64_t w_stage;
 };
@@ -645,6 +761,7 @@ FD_DEV Ring carve_ring(unsigned char* smem_raw, int S, int B, int x_slot, int64_
   r.xchg = reinterpret_cast<float*>(r.xreg + ((x_bytes + 15) & ~15ll));
   r.full = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(r.xchg) + (BR / 2) * MT_MAX * 4);
   r.empty = r.full + MAX_STAGES;
+  r.fin = reinterpret_cast<float*>(r.empty + MAX_STAGES);
   return r;
 }
 
@@ -1102,13 +1219,18 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
         if (threadIdx.x == 0) {
           *s_last = *reinterpret_cast<volatile int*>(ms.fast) == ms.tag;
           *reinterpret_cast<volatile int*>(ms.decided) = ms.tag;
+          __threadfence_block();  // the flag before the staged partials
         }
         consumer_sync();
         if (*s_last) {
           // every other contributor has published: this CTA completes the
           // block without publishing its own partial
-          __threadfence();
-          reduce_block<T, NT, MODE>(a, cb, r.xchg, G, ex, &acc, c);
+          if (fin_staged<NT>(a, s1, G, c)) {
+            reduce_staged<T, NT, MODE>(a, cb, r.fin, r.xchg, G, ex, acc, c);
+          } else {
+            __threadfence();
+            reduce_block<T, NT, MODE>(a, cb, r.xchg, G, ex, &acc, c);
+          }
         } else {
           write_slot<NT>(a, cb == s0 / a.ks ? 0 : 1, acc, c);
           settle<T, NT, MODE>(a, cb, r.xchg, G, s_last);
