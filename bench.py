@@ -415,16 +415,31 @@ def run_ops(torch, device, roof_gbs: float, peak_gbs: float) -> dict:
             rec(f"swiglu_{rows}x{I}_{tag}", graph_time_us(torch, calls), nb,
                 check=lambda: (fd.swiglu(gs[0], us_[0]), R.swiglu_reference(gs[0], us_[0])))
             del gs, us_, os_
-    # RoPE (config 1): x [1, T, 32, 128], cos/sin [T, 1, 128] from theta = 500000
-    for t in (2048, 1):
+    # RoPE (config 1): x [1, T, 32, 128], cos/sin [T, 1, 128] from theta = 500000;
+    # T = 16384 is the large shape (277 MB) beside the configuration's 2048 (35 MB).
+    # Beside each row: a plain copy of the same bytes (half in, half out) timed the
+    # same way, i.e. the fixed launch, ramp and drain cost a kernel of that size pays.
+    from fused_decode_b200 import kernels as K
+    for t in (2048, 16384, 1):
         cos, sin = rope_tables(torch, t, 128, device, f16)
         nb = 2 * t * 32 * 128 * 2 + 2 * t * 128 * 2
         k = copies_for(nb)
         xs = [torch.randn(1, t, 32, 128, device=device, dtype=f16, generator=g) for _ in range(k)]
         os_ = [torch.empty_like(xs[0]) for _ in range(k)]
         calls = [(lambda j=j: fd.rope(xs[j], cos, sin, out=os_[j])) for j in range(k)]
-        rec(f"rope_1x{t}x32x128_f16", graph_time_us(torch, calls), nb,
-            check=lambda: (fd.rope(xs[0], cos, sin), R.rope_reference(xs[0], cos, sin)))
+        extra = {}
+        if t > 1:
+            n_half = nb // 4  # bf16 elements of each side of a copy moving nb bytes
+            srcs = [torch.empty(n_half, device=device, dtype=torch.bfloat16) for _ in range(k)]
+            dsts = [torch.empty_like(srcs[0]) for _ in range(k)]
+            copy_us = graph_time_us(torch, [(lambda j=j: K.launch_copy(dsts[j], srcs[j])) for j in range(k)])
+            rope_us = graph_time_us(torch, calls)
+            extra = {"same_size_copy_us": copy_us, "frac_same_size_copy": copy_us / rope_us}
+            del srcs, dsts
+        else:
+            rope_us = graph_time_us(torch, calls)
+        rec(f"rope_1x{t}x32x128_f16", rope_us, nb,
+            check=lambda: (fd.rope(xs[0], cos, sin), R.rope_reference(xs[0], cos, sin)), **extra)
         del xs, os_
     # linear_decode sweep (config 2); weights rotate through >= 2x L2
     for dt, tag in ((torch.bfloat16, "bf16"), (f16, "f16")):
@@ -569,6 +584,17 @@ def run_tp_block(torch, device, world, rank, args, pk, barrier, max_over_ranks) 
         gbs = nb * LAYERS70 / (us * 1e-6) / 1e9
         per_m[f"m{m}"] = {"us_per_step": us, "us_per_layer": us / LAYERS70, "bytes_per_layer_per_gpu": nb,
                           "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / pk["hbm_gbs"]}
+
+        if m == 1 and exchange is not None:
+            # the opt-in rank sum in the down projection's epilogue (two
+            # launches a layer) beside the default's reduce kernel
+            os.environ["FD_TP_FOLD"] = "1"  # read by the library at each layer call
+            try:
+                graph, _ = capture(block, x0)
+                per_m["m1"]["us_per_layer_tp_fold"] = time_graph(graph, steps) / LAYERS70
+                del graph
+            finally:
+                del os.environ["FD_TP_FOLD"]
 
         if m == 1:
             # the same layer's pieces, each as 80 launches in one graph
@@ -744,6 +770,19 @@ def run_ours(args) -> None:
         finally:
             del os.environ["FD_STACK_PERSISTENT"]
 
+    # ---- tensor parallel: the opt-in rank sum in the down projection's
+    # epilogue (two launches a layer) beside the default's reduce kernel
+    fold_us = None
+    if exchange is not None:
+        os.environ["FD_TP_FOLD"] = "1"  # read by the library at each layer call
+        try:
+            stack_f = MlpStack(layers, args.m, EPS, kind="dot", exchange=exchange)
+            ms_f, _ = time_stack(stack_f, max(3, args.steps // 5), args.warmup)
+            fold_us = ms_f * 1e3 / LAYERS
+            del stack_f
+        finally:
+            del os.environ["FD_TP_FOLD"]
+
     # ---- the same stack as two stream-K kernels per layer (gate/up, then down + residual)
     two_kernel_us = None
     if world == 1:
@@ -898,6 +937,7 @@ def run_ours(args) -> None:
                 "per_layer_calls_us_per_layer": per_layer_us,
                 "persistent_kernel_us_per_layer": persistent_us,
                 "two_kernel_us_per_layer": two_kernel_us,
+                "tp_fold_us_per_layer": fold_us,
             },
             "ops": ops,
             "ops_parity_ok": (all(r.get("parity_ok", True) for r in ops.values()) if ops else None),

@@ -105,11 +105,18 @@ STACK_MIN_LAUNCH_REGS = 160
 
 
 def _check_stack_registers(ptxas_log: str) -> None:
+    """The persistent stack kernel launches with enough registers for its
+    setmaxnreg split, and its one-tile (batch <= 8, NT = 1) instantiations do
+    not spill: their prologue and stream share the consumer warps' budget."""
     entry = None
     seen = 0
     for line in ptxas_log.splitlines():
         if "Compiling entry function" in line:
             entry = line
+        elif entry and "spill stores" in line and "mlp_stack_kernel" in entry and "Li1ELb" in entry:
+            spilled = int(line.split("bytes spill stores")[0].split(",")[-1])
+            if spilled:
+                raise RuntimeError(f"mlp_stack_kernel (NT = 1) spills {spilled} bytes: {entry}")
         elif entry and "Used" in line and "registers" in line:
             if "mlp_stack_kernel" in entry:
                 regs = int(line.split("Used")[1].split("registers")[0])

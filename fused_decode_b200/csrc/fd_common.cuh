@@ -185,6 +185,14 @@ FD_DEV float warp_sum(float v) {
 // s - 2 carries tag s - 1).
 constexpr int kMaxTpWorld = 8;
 constexpr int kTpBlockRows = 128;
+constexpr int kStatusTpTimeout = 8;  // status bit: a wait for a peer's word expired
+
+// A tagged word as a peer stored it (an NVLink store into this buffer).
+FD_DEV uint2 ld_tagged_sys(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
 
 struct TpLayout {
   int64_t nblk, data_off, bytes;

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
         bulk_load(nw_smem, a.norm_w, nb, &s_nw_bar);
       }
       prefetch_map(&wmap);
-      if (MODE == MODE_LINEAR) prefetch_map(&xmap);
+      if (linear_mode(MODE)) prefetch_map(&xmap);
       produce_phase<MODE>(r, &wmap, &xmap, a, s0, s1, 0, p, P, evict_first_policy(), &s_abort, [] {
         grid_dep_wait();  // the activation is the previous kernel's output
         return true;
@@ -114,7 +114,7 @@ __host__ __device__ inline size_t cluster_part_bytes(int split) {
   return static_cast<size_t>(split - 1) * BR * kPartStride * sizeof(float);
 }
 
-template <typename T, int NT, int KIND, int MP>
+template <typename T, int NT, int KIND, int MP, int MODE>
 __global__ void __launch_bounds__(kClusterThreads, 1)
     gemv_cluster_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                         const GemvArgs a) {
@@ -165,12 +165,12 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
     // The leader's epilogue terms (bias, residual rows) are inputs: load them
     // now, so their L2 round trip overlaps the weight stream instead of
     // following the partials' arrival at the end.
-    if (rank == 0) Epilogue<T, NT, MODE_LINEAR>::extras(a, blk, ex);
+    if (rank == 0) Epilogue<T, NT, MODE>::extras(a, blk, ex);
     grid_dep_launch();
     // Phase 1 complete (every CTA of the cluster is running): waited here,
     // where the first stage's latency hides it, not after the stream.
     cluster_wait();
-    consume_phase<T, NT, KIND, MP, MODE_LINEAR>(a, r, s0, s1, 0, 1, 0, &s_last, &s_abort, ms, &acc);
+    consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, 1, 0, &s_last, &s_abort, ms, &acc);
   }
   if (warp >= GW) {
     cluster_wait();  // phase 1 (long complete): every thread takes part in each arrive / wait pair
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
         sum.v[t][2 * h + 1] += v.y;
       }
   }
-  Epilogue<T, NT, MODE_LINEAR>::run(a, blk, sum, ex, r.xchg);
+  Epilogue<T, NT, MODE>::run(a, blk, sum, ex, r.xchg);
 }
 
 // ------------------------------------------------------------ generic GEMV
@@ -297,11 +297,15 @@ cudaError_t dispatch_tma(const CUtensorMap& wm, const CUtensorMap& xm, const Gem
     if (a.m <= 8) return L(gemv_tma_kernel<T, 1, 0, 1, MODE, MT1, 1>);
     return L(gemv_tma_kernel<T, 2, 0, 1, MODE, MT1, 1>);
   }
-  if (a.m <= 1) return L(gemv_tma_kernel<T, 1, 1, 1, MODE, MT1, 1>);
-  if (a.m <= 2) return L(gemv_tma_kernel<T, 1, 1, 2, MODE, MT1, 1>);
-  if (a.m <= 4) return L(gemv_tma_kernel<T, 1, 1, 4, MODE, MT1, 1>);
-  if (a.m <= 8) return L(gemv_tma_kernel<T, 1, 1, 8, MODE, MT1, 1>);
-  return L(gemv_tma_kernel<T, 2, 1, 16, MODE, MT1, 1>);
+  if constexpr (MODE == MODE_LINEAR_TP) {
+    return cudaErrorInvalidValue;  // dot only (launch_linear)
+  } else {
+    if (a.m <= 1) return L(gemv_tma_kernel<T, 1, 1, 1, MODE, MT1, 1>);
+    if (a.m <= 2) return L(gemv_tma_kernel<T, 1, 1, 2, MODE, MT1, 1>);
+    if (a.m <= 4) return L(gemv_tma_kernel<T, 1, 1, 4, MODE, MT1, 1>);
+    if (a.m <= 8) return L(gemv_tma_kernel<T, 1, 1, 8, MODE, MT1, 1>);
+    return L(gemv_tma_kernel<T, 2, 1, 16, MODE, MT1, 1>);
+  }
 }
 
 // Cluster size for a LINEAR launch, 0 for stream-K: the largest S in {4, 2}
@@ -366,24 +370,30 @@ cudaError_t launch_cluster(Kern kern, const CUtensorMap& wm, const CUtensorMap& 
   return cudaLaunchKernelEx(&cfg, kern, wm, xm, a);
 }
 
-template <typename T>
+template <typename T, int MODE>
 cudaError_t dispatch_cluster(const CUtensorMap& wm, const CUtensorMap& xm, const GemvArgs& a, int kind, size_t smem,
                              cudaStream_t st) {
   auto L = [&](auto kern) { return launch_cluster(kern, wm, xm, a, smem, st); };
   if (kind == FD_KIND_DOT) {
-    if (a.m <= 8) return L(gemv_cluster_kernel<T, 1, 0, 1>);
-    return L(gemv_cluster_kernel<T, 2, 0, 1>);
+    if (a.m <= 8) return L(gemv_cluster_kernel<T, 1, 0, 1, MODE>);
+    return L(gemv_cluster_kernel<T, 2, 0, 1, MODE>);
   }
-  if (a.m <= 1) return L(gemv_cluster_kernel<T, 1, 1, 1>);
-  if (a.m <= 2) return L(gemv_cluster_kernel<T, 1, 1, 2>);
-  if (a.m <= 4) return L(gemv_cluster_kernel<T, 1, 1, 4>);
-  if (a.m <= 8) return L(gemv_cluster_kernel<T, 1, 1, 8>);
-  return L(gemv_cluster_kernel<T, 2, 1, 16>);
+  if constexpr (MODE == MODE_LINEAR_TP) {
+    return cudaErrorInvalidValue;  // dot only (launch_linear)
+  } else {
+    if (a.m <= 1) return L(gemv_cluster_kernel<T, 1, 1, 1, MODE>);
+    if (a.m <= 2) return L(gemv_cluster_kernel<T, 1, 1, 2, MODE>);
+    if (a.m <= 4) return L(gemv_cluster_kernel<T, 1, 1, 4, MODE>);
+    if (a.m <= 8) return L(gemv_cluster_kernel<T, 1, 1, 8, MODE>);
+    return L(gemv_cluster_kernel<T, 2, 1, 16, MODE>);
+  }
 }
 
 // Launch the stream-K TMA GEMV in LINEAR mode: y = x @ w^T (+bias)(+row_add).
+// tp_fold: the tensor-parallel epilogue that also sums the ranks
+// (MODE_LINEAR_TP, kind = dot only).
 int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvArgs a, int dtype, int kind,
-                  const Workspace& ws, cudaStream_t st) {
+                  const Workspace& ws, cudaStream_t st, bool tp_fold = false) {
   const int m = a.m;
   const Geometry geo = choose_geometry([m](int stages, int boxes) { return linear_x_bytes(m, stages, boxes); });
   if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
@@ -405,16 +415,20 @@ int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvAr
     a.cl_split = split;
     const size_t csmem =
         ring_smem_bytes(linear_x_bytes(a.m, a.stages, a.boxes) + cluster_part_bytes(split), a.stages, a.boxes);
-    cudaError_t e = dtype == FD_BF16 ? dispatch_cluster<__nv_bfloat16>(wm, xm, a, kind, csmem, st)
-                                     : dispatch_cluster<__half>(wm, xm, a, kind, csmem, st);
+    cudaError_t e = tp_fold ? (dtype == FD_BF16 ? dispatch_cluster<__nv_bfloat16, MODE_LINEAR_TP>(wm, xm, a, kind, csmem, st)
+                                                : dispatch_cluster<__half, MODE_LINEAR_TP>(wm, xm, a, kind, csmem, st))
+                            : (dtype == FD_BF16 ? dispatch_cluster<__nv_bfloat16, MODE_LINEAR>(wm, xm, a, kind, csmem, st)
+                                                : dispatch_cluster<__half, MODE_LINEAR>(wm, xm, a, kind, csmem, st));
     if (e == cudaSuccess) return FD_OK;
     if (e != cudaErrorUnsupportedLimit) return FD_ERR_LAUNCH;
     (void)cudaGetLastError();  // the clusters do not fit the device: stream-K below
     a.cl_split = 0;
   }
   const size_t smem = ring_smem_bytes(linear_x_bytes(a.m, a.stages, a.boxes), a.stages, a.boxes);
-  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st)
-                                   : dispatch_tma<__half, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st);
+  cudaError_t e = tp_fold ? (dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR_TP>(wm, xm, a, kind, geo, smem, st)
+                                              : dispatch_tma<__half, MODE_LINEAR_TP>(wm, xm, a, kind, geo, smem, st))
+                          : (dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st)
+                                              : dispatch_tma<__half, MODE_LINEAR>(wm, xm, a, kind, geo, smem, st));
   return from_cuda(e);
 }
 
@@ -620,6 +634,12 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
   b.tp_rank = rank; b.tp_world = world; b.tp_mmax = m_max;
   b.tp_data_off = l.data_off;
   b.tp_seq = static_cast<const int*>(exchange[rank]);
+  if (kind == FD_KIND_DOT && tp_fold_enabled()) {
+    // opt-in, two launches: each block's finisher also sums the ranks and adds the residual
+    b.ra = hidden; b.ra_dtype = dtype; b.srm = h; b.srn = 1;
+    b.y = static_cast<char*>(out); b.sym = h; b.syn = 1;
+    return launch_linear(mid, i, w_down, s_down, b, dtype, kind, ws, st, true);
+  }
   r = launch_linear(mid, i, w_down, s_down, b, dtype, kind, ws, st);
   if (r != FD_OK) return r;
   return tp_reduce_launch(static_cast<char*>(exchange[rank]), world, m, m_max, h, hidden, out, dtype, ws.status, st);
@@ -652,7 +672,7 @@ int fd_post_attn_mlp_tp_stack_out(const void* hidden, int32_t layers, const void
                                       dtype, m, h, i, eps, kind, ws, ws.tail, ping[0], ping[1], st, rank, world,
                                       exchange, m_max);
   if (rp != FD_ERR_UNSUPPORTED) return rp;
-  // three launches per layer (fd_post_attn_mlp_tp_out)
+  // three launches per layer (two with FD_TP_FOLD=1): fd_post_attn_mlp_tp_out
   const void* cur = hidden;
   for (int l = 0; l < layers; ++l) {
     void* dst = l == layers - 1 ? out : ping[l & 1];

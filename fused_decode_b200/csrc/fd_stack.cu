@@ -55,7 +55,6 @@ constexpr int kConsumerRegs = 208;
 constexpr int kHelperRegs = 56;
 static_assert(8 * 32 * kConsumerRegs + 4 * 32 * kHelperRegs <= kStackThreads * 160, "register split");
 constexpr int kStatusBarrierTimeout = 16;
-constexpr int kStatusTpTimeout = 8;  // as the tensor-parallel reduce kernel
 constexpr size_t kBarOffset = 128;  // barrier counter: inside the status area, its own 128-byte line
 constexpr int kDepartOffset = 16;   // departure counter: 16 ints after the barrier counter
 
@@ -77,12 +76,6 @@ struct StackParams {
   int xact_bytes;   // activation part of the X region; the norm weight follows it
   int x_bytes;
 };
-
-FD_DEV uint2 ld_tagged_sys(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
-}
 
 FD_DEV bool phase_wait(const int* bar, int target, int* status, int* s_abort) {
   if (ld_acquire_gpu(bar) >= target) return true;
@@ -338,7 +331,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) mlp_stack_kernel(const __gri
     if (ph > 0 && !consumer_phase_wait(p.bar, static_cast<int>(gridDim.x) * ph, status, &s_abort)) break;
     if (threadIdx.x == 0) s_hidden = gl == 0 ? p.hidden : p.ping[(gl - 1) & 1];
     consumer_sync();
-    norm_to_smem<T>(ga, *reinterpret_cast<const void* volatile*>(&s_hidden), r, s_sumsq, nw_smem, &s_nw_full,
+    norm_to_smem<T, 1>(ga, *reinterpret_cast<const void* volatile*>(&s_hidden), r, s_sumsq, nw_smem, &s_nw_full,
                     static_cast<uint32_t>(l & 1));
     if (threadIdx.x == 0) mbar_arrive(&s_nw_empty);
     if (!consume_phase<T, NT, 0, 1, MODE_GATEUP>(ga, r, rng[0], rng[1], base, rng[4], blockIdx.x, &s_last,
@@ -543,7 +536,8 @@ extern "C" int fd_post_attn_mlp_tp_stack_launches(int32_t layers, int32_t norm_d
   const bool persistent =
       kind == FD_KIND_DOT && m <= MT_MAX &&
       fd_host::persistent_wanted(true, stack_geometry(m, h, i, norm_dtype == FD_F32 ? 4 : 2, fd_host::sm_count()));
-  return persistent ? (layers + kStackMaxLayers - 1) / kStackMaxLayers : 3 * layers;
+  if (persistent) return (layers + kStackMaxLayers - 1) / kStackMaxLayers;
+  return (kind == FD_KIND_DOT && fd_host::tp_fold_enabled() ? 2 : 3) * layers;
 }
 
 extern "C" int fd_post_attn_mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,

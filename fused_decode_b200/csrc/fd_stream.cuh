@@ -65,7 +65,11 @@ constexpr int kStatusEmptyTimeout = 2;
 // LINEAR_X: a GEMV whose activation columns for the CTA's step range were
 // staged in shared memory by the consumers (the persistent MLP stack's down
 // projection: its activation is written inside the same kernel).
-enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2 };
+// MODE_LINEAR_TP: LINEAR whose epilogue also sums the tensor-parallel ranks
+// (tp_fold_block) -- its own instantiations, so the plain LINEAR kernels
+// carry none of that code.
+enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2, MODE_LINEAR_TP = 3 };
+__host__ __device__ constexpr bool linear_mode(int mode) { return mode == MODE_LINEAR || mode == MODE_LINEAR_TP; }
 
 // One phase of streaming: a GEMV (LINEAR) or the MLP gate/up stage (GATEUP).
 struct GemvArgs {
@@ -322,6 +326,87 @@ FD_DEV void tp_publish(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, int s
   }
 }
 
+// Tensor parallel with the rank sum folded into the down projection: after
+// publishing block blk, the CTA that finished it waits (bounded) for every
+// other rank's tagged words of the same elements in this rank's buffer, sums
+// the ranks in rank order -- its own partial from registers, the very value
+// it published -- adds the residual `ex` and rounds into y: the bits
+// tp_reduce_kernel would produce, without its launch.  The last block
+// finished on this rank advances the round number.  All consumer threads.
+// A thread's elements go in two batches of one column parity each (rows g
+// and g + 8), every rank's word of a batch requested before any is checked:
+// one round trip per batch, and none for a batch past the last column (at
+// M = 1 the odd columns), with half the loads in flight a whole tile would
+// hold in registers.
+template <typename T, int NT>
+FD_DEV void tp_fold_block(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& ex, int seq) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int world = a.tp_world, me = a.tp_rank;
+  const int64_t rank_stride = static_cast<int64_t>(a.tp_mmax) * a.n;
+  const uint2* base = reinterpret_cast<const uint2*>(a.tp_peer[me] + a.tp_data_off) +
+                      static_cast<int64_t>((seq & 1) * world) * rank_stride;
+  const uint32_t tag = static_cast<uint32_t>(seq + 1);
+  bool ok = true;
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int par = 0; par < 2; ++par) {
+      const int col = 8 * t + 2 * q + par;
+      if (col >= a.m) continue;
+      int64_t off[2];
+      bool valid[2];
+      uint2 v[2][kMaxTpWorld];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t row = blk * BR + 16 * warp + g + 8 * h;
+        valid[h] = row < a.n;
+        off[h] = col * a.n + row;
+#pragma unroll
+        for (int rk = 0; rk < kMaxTpWorld; ++rk)
+          v[h][rk] = (valid[h] && rk < world && rk != me) ? ld_tagged_sys(base + rk * rank_stride + off[h])
+                                                          : make_uint2(0u, tag);
+      }
+      const uint64_t t0 = globaltimer();
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int rk = 0; rk < kMaxTpWorld; ++rk)
+          while (ok && v[h][rk].y != tag) {
+            if (globaltimer() - t0 > kWaitNs) {
+              atomicOr(a.status, kStatusTpTimeout);
+              ok = false;
+              break;
+            }
+            __nanosleep(32);
+            v[h][rk] = ld_tagged_sys(base + rk * rank_stride + off[h]);
+          }
+      if (!ok) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!valid[h]) continue;
+        const int e = 2 * h + par;
+        float sum = 0.f;
+#pragma unroll
+        for (int rk = 0; rk < kMaxTpWorld; ++rk)  // rank order: the same sum on every rank
+          if (rk < world) sum += rk == me ? acc.v[t][e] : __uint_as_float(v[h][rk].x);
+        sum += ex.v[t][e];
+        const int64_t row = blk * BR + 16 * warp + g + 8 * h;
+        reinterpret_cast<T*>(a.y)[col * a.sym + row * a.syn] = from_f32<T>(sum);
+      }
+    }
+  // every consumer thread has read the round number: count the block
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    int* seqp = reinterpret_cast<int*>(a.tp_peer[me]);
+    __threadfence();
+    if (atomicAdd(seqp + 1, 1) == static_cast<int>(a.nblocks) - 1) {
+      seqp[1] = 0;
+      *reinterpret_cast<volatile int*>(seqp) = seq + 1;
+    }
+  }
+}
+
 template <typename T, int NT, int MODE>
 struct Epilogue;
 
@@ -371,6 +456,21 @@ struct Epilogue<T, NT, MODE_LINEAR> {
         }
       }
     }
+  }
+};
+
+// Tensor parallel with the rank sum folded in: publish the block's partial
+// to every rank, then sum the ranks' words + the residual (`ex`, from ra)
+// into y (tp_fold_block).
+template <typename T, int NT>
+struct Epilogue<T, NT, MODE_LINEAR_TP> {
+  FD_DEV static void extras(const GemvArgs& a, int64_t blk, Acc<NT>& ex) {
+    Epilogue<T, NT, MODE_LINEAR>::extras(a, blk, ex);
+  }
+  FD_DEV static void run(const GemvArgs& a, int64_t blk, const Acc<NT>& acc, const Acc<NT>& ex, float* /*xchg*/) {
+    const int seq = *reinterpret_cast<const volatile int*>(a.tp_seq);
+    tp_publish(a, blk, acc, seq);
+    tp_fold_block<T, NT>(a, blk, acc, ex, seq);
   }
 };
 
@@ -775,7 +875,7 @@ FD_DEV void ring_init(const Ring& r) {
 
 template <int MODE>
 FD_DEV uint32_t stage_bytes(const Ring& r, const GemvArgs& a) {
-  return static_cast<uint32_t>(r.w_stage) + (MODE == MODE_LINEAR ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
+  return static_cast<uint32_t>(r.w_stage) + (linear_mode(MODE) ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
 }
 
 // Weight boxes of phase step t into ring index gi.
@@ -831,7 +931,7 @@ FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensor
     mbar_expect_tx(&r.full[gi % r.S], sb);
     issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
   }
-  if (MODE == MODE_LINEAR) {
+  if (linear_mode(MODE)) {
     if (!ready()) return false;
     for (int64_t g2 = first; g2 < base + npre; g2 += P) issue_x(r, xmap, a, s0 + (g2 - base), g2);
   }
@@ -839,7 +939,7 @@ FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensor
     if (!acquire(gi)) return false;
     mbar_expect_tx(&r.full[gi % r.S], sb);
     issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
-    if (MODE == MODE_LINEAR) issue_x(r, xmap, a, s0 + (gi - base), gi);
+    if (linear_mode(MODE)) issue_x(r, xmap, a, s0 + (gi - base), gi);
   }
   return true;
 }
@@ -1046,18 +1146,20 @@ FD_DEV void norm_rows(const GemvArgs& a, const void* hidden, const Ring& r, floa
 
 // `hidden`: the rows to normalise (a.hidden for a single launch; the stack
 // passes each layer's input).  The row block RB is the batch rounded up to
-// 1, 2, 4 or 8 (batches above 8 take two blocks).
-template <typename T>
+// 1, 2, 4 or 8, at most RBMAX (larger batches take several blocks): a kernel
+// whose consumer warps hold more state across the prologue (the persistent
+// stack) takes a smaller block rather than spill.
+template <typename T, int RBMAX = 8>
 FD_DEV void norm_to_smem(const GemvArgs& a, const void* hidden, const Ring& r, float (*s_sumsq)[MT_MAX],
                          const unsigned char* nw, uint64_t* nw_bar, uint32_t nw_parity = 0) {
-  if (a.m == 1)
+  if (a.m == 1 || RBMAX == 1)
     norm_rows<T, 1>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
-  else if (a.m == 2)
+  else if (a.m == 2 || RBMAX == 2)
     norm_rows<T, 2>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
-  else if (a.m <= 4)
-    norm_rows<T, 4>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
+  else if (a.m <= 4 || RBMAX == 4)
+    norm_rows<T, (RBMAX < 4 ? RBMAX : 4)>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
   else
-    norm_rows<T, 8>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
+    norm_rows<T, (RBMAX < 8 ? RBMAX : 8)>(a, hidden, r, s_sumsq, nw, nw_bar, nw_parity);
 }
 
 // Consumer warps' share of one phase: phase steps [s0, s1) at ring indices
@@ -1102,7 +1204,7 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
     }
     // activation box j of this step: [m rows x 128 B] (swizzled by row & 7)
     auto xbox = [&](int j) -> const unsigned char* {
-      if (MODE == MODE_LINEAR) return r.xreg + (s * B + j) * r.x_slot;
+      if (linear_mode(MODE)) return r.xreg + (s * B + j) * r.x_slot;
       if (MODE == MODE_LINEAR_X) return r.xreg + ((it * B + j) * a.m) * 128;
       return r.xreg + ((ck * B + j) * a.m) * 128;
     };
@@ -1396,4 +1498,16 @@ int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* 
                          int32_t tp_rank = 0, int32_t tp_world = 0, void* const* exchange = nullptr,
                          int32_t tp_mmax = 0);
 int mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i, int32_t kind);
+
+// Tensor parallel: with FD_TP_FOLD=1 (and kind = dot) the rank sum runs in
+// the down projection's epilogue (tp_fold_block, two launches a layer);
+// otherwise in the separate tp_reduce_kernel launch (three a layer).  The
+// default is the separate kernel: on 2 and 4 B200s the fold measured as fast
+// or slightly slower -- it saves a launch, but each block's finishing CTA
+// then holds its SM's shared memory while it waits for the peers, and the
+// next layer's gate/up CTAs cannot start their weight prefetch there.
+inline bool tp_fold_enabled() {
+  const char* env = std::getenv("FD_TP_FOLD");
+  return env && env[0] == '1';
+}
 }  // namespace fd_host

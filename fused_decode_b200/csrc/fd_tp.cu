@@ -20,7 +20,6 @@ using namespace fd;
 namespace {
 
 constexpr uint64_t kTpWaitNs = 2000000000ull;  // bounded flag waits: 2 s
-constexpr int kStatusTpTimeout = 8;
 
 FD_DEV uint64_t gtimer() {
   uint64_t t;
@@ -36,12 +35,6 @@ struct TpReduceArgs {
   void* out;        // [m, n] (contiguous)
   int* status;
 };
-
-FD_DEV uint2 ld_tagged_sys(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
-}
 
 // One thread per (row, column): grid (row blocks of 128, m).  The words of
 // all ranks are loaded together (one round trip), then any whose tag is not

@@ -403,8 +403,8 @@ def post_attn_mlp_tp_stack_out(
 ) -> None:
     """``len(layers)`` tensor-parallel MLP layers ``(norm_weight, w_gate_up
     shard, w_down shard)`` enqueued by one library call (three launches per
-    layer, or one persistent kernel per 32 layers under
-    FD_STACK_PERSISTENT=1) whose partial sums travel through the NVLink
+    layer, two under FD_TP_FOLD=1, or one persistent kernel per 32 layers
+    under FD_STACK_PERSISTENT=1) whose partial sums travel through the NVLink
     exchange buffers of ``exchange``; the last output lands in ``out2`` on
     every rank."""
     if not layers:

@@ -10,7 +10,8 @@ layer, or one persistent kernel per 32 layers with FD_STACK_PERSISTENT=1;
 intermediates in the library workspace).  With ``exchange=`` (a
 ``fused_decode_b200.tp.TPExchange``) the layers are this rank's
 tensor-parallel shards and the call is ``fd_post_attn_mlp_tp_stack_out``
-(three launches per layer, or one persistent kernel with the rank reduction
+(three launches per layer, two with the rank sum in the down projection's
+epilogue under FD_TP_FOLD=1, or one persistent kernel with the rank reduction
 inside it under FD_STACK_PERSISTENT=1).  ``fused=False`` captures one
 ``post_attn_mlp`` call per layer instead, and ``layer_fn`` captures any per-layer callable (the
 tensor-parallel layer of ``fused_decode_b200.tp``, for one).

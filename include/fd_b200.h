@@ -232,7 +232,9 @@ int fd_tp_exchange_close(void* peer);
  * world device pointers: this rank's buffer at [rank], the mapped peer
  * buffers elsewhere) -- and a kernel that waits (bounded) for all ranks'
  * partials, sums them in rank order and writes out = round(sum + hidden),
- * the same bits on every rank.  A wait that expires sets bit 8 of the
+ * the same bits on every rank.  With FD_TP_FOLD=1 in the environment and
+ * kind = FD_KIND_DOT, the CTA that finishes a block of the down projection
+ * does that sum for its block instead: two launches, the same bits.  A wait that expires sets bit 8 of the
  * workspace status word.  Workspace: fd_post_attn_mlp_workspace_bytes(m, h, i). */
 int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm_dtype,
                             const void* w_gate_up, int64_t s_gu,
@@ -247,13 +249,13 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
  * fd_post_attn_mlp_tp_out, with norm_w, w_gate_up (this rank's [2*i, h]
  * restacks) and w_down (its [h, i] column slices) as HOST arrays of device
  * pointers; only the last layer's output is written to `out`, every rank
- * getting the same bits.  Three launches per layer; with FD_STACK_PERSISTENT=1
+ * getting the same bits.  Three launches per layer (two with FD_TP_FOLD=1); with FD_STACK_PERSISTENT=1
  * in the environment and kind = FD_KIND_DOT (where the batch leaves at
  * least 4 ring stages), one persistent cooperative kernel per 32 layers -- per layer a gate/up phase, a down
  * phase whose block partials go to every rank's exchange buffer, and a
  * phase that sums the ranks' partials (bounded waits, status bit 8) and adds
  * the residual -- with no launch between layers (measured slower than the
- * three launches on 2 B200s, so not the default).  The same exchange and
+ * per-layer launches on 2 B200s, so not the default).  The same exchange and
  * round-counting rules as
  * fd_post_attn_mlp_tp_out.  Workspace: fd_post_attn_mlp_workspace_bytes(m, h, i). */
 /* Kernel launches one fd_post_attn_mlp_tp_stack_out call of this shape makes

@@ -178,17 +178,22 @@ def test_tp_decode_block_llama70b(m):
     torch.testing.assert_close(out.float().cpu(), torch.from_numpy(ref), **TOL)
 
 
+@pytest.mark.parametrize("fold", ["1", "0"])
+@pytest.mark.parametrize("h", [1024, 4096])
 @pytest.mark.parametrize("m", [1, 5, 16])
-def test_tp_exchange_single_rank(m):
+def test_tp_exchange_single_rank(m, h, fold, monkeypatch):
     """The NVLink-exchange layer (down-projection partials published into the
-    exchange buffer, then the reduce kernel) with a group of one: equal bit
-    for bit to post_attn_mlp, round after round (the buffer's two parities
-    alternate), inside a CUDA graph too, and the status word stays clear."""
+    exchange buffer; the rank sum in a separate kernel, or with FD_TP_FOLD=1
+    in the down projection's epilogue) with a group of one: equal bit for bit
+    to post_attn_mlp, round after round (the buffer's two parities
+    alternate), inside a CUDA graph too, and the status word stays clear.
+    h = 1024 splits the down projection stream-K, h = 4096 by clusters."""
     from fused_decode_b200 import kernels as K
     from fused_decode_b200 import post_attn_mlp
     from fused_decode_b200.stack import MlpStack
 
-    h, i = 1024, 2816
+    monkeypatch.setenv("FD_TP_FOLD", fold)
+    i = 2816
     ex = tp.TPExchange(h, m_max=16)
     try:
         layers = [_layer(h, i, m, 900 + l)[1:] for l in range(3)]
@@ -200,13 +205,10 @@ def test_tp_exchange_single_rank(m):
             got = mod(x)
             want = post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot")
             assert torch.equal(got, want), rnd
+            # each round within the parity bar of the oracle on its own input
+            ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), EPS, "bfloat16")
+            torch.testing.assert_close(got.float().cpu(), torch.from_numpy(ref), **TOL)
             x = got
-        ref = _np(x0)
-        for rnd in range(5):
-            nw, wgu, wd = layers[rnd % 3]
-            ref = O.post_attn_mlp(ref, _np(nw), _np(wgu), _np(wd), EPS, "bfloat16")
-        # five chained layers: a one-ulp difference can grow, so twice the per-layer tolerance
-        torch.testing.assert_close(x.float().cpu(), torch.from_numpy(ref), rtol=2e-2, atol=2e-2)
 
         def fn(t, nw, wgu, wd):
             return tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)(t)
@@ -225,6 +227,36 @@ def test_tp_exchange_single_rank(m):
         ex.close()
 
 
+@pytest.mark.parametrize("m", [1, 8])
+def test_tp_exchange_modes_interleaved(m, monkeypatch):
+    """Layers alternating between the folded rank sum and the separate reduce
+    kernel on one exchange buffer (group of one): both advance the same round
+    number, so every layer matches post_attn_mlp bit for bit, and the stack
+    entry point enqueues two launches per layer folded, three otherwise."""
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200 import post_attn_mlp
+    from fused_decode_b200.stack import MlpStack
+
+    h, i = 4096, 2816
+    ex = tp.TPExchange(h, m_max=16)
+    try:
+        layers = [_layer(h, i, m, 1200 + l)[1:] for l in range(2)]
+        x = _layer(h, i, m, 1250)[0]
+        for rnd in range(6):
+            monkeypatch.setenv("FD_TP_FOLD", "01"[rnd % 2])
+            nw, wgu, wd = layers[rnd % 2]
+            got = tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)(x)
+            assert torch.equal(got, post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot")), rnd
+            x = got
+        for fold, per_layer in (("1", 2), ("0", 3)):
+            monkeypatch.setenv("FD_TP_FOLD", fold)
+            assert MlpStack(layers, m, EPS, kind="dot", exchange=ex).launches_per_replay == per_layer * len(layers)
+        torch.cuda.synchronize()
+        assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+    finally:
+        ex.close()
+
+
 def _rank_main_nvlink(rank, world, port, outdir, h, i, m, layers):
     import torch.distributed as dist
 
@@ -237,13 +269,18 @@ def _rank_main_nvlink(rank, world, port, outdir, h, i, m, layers):
     try:
         dev = torch.device("cuda", rank)
         ex = tp.TPExchange(h, m_max=16)
-        x = None
-        for layer in range(layers):
-            x0, nw, wgu, wd = _layer(h, i, m, 500 + layer, device=dev)
-            x = x0 if x is None else x
-            x = tp.TPPostAttnMlp.from_full(nw, wgu, wd, rank, world, EPS, kind="dot", exchange=ex)(x)
+        res = []
+        for fold in ("1", "0"):  # rank sum in the down epilogue, then as its own kernel
+            os.environ["FD_TP_FOLD"] = fold
+            x, outs = None, []
+            for layer in range(layers):
+                x0, nw, wgu, wd = _layer(h, i, m, 500 + layer, device=dev)
+                x = x0 if x is None else x
+                x = tp.TPPostAttnMlp.from_full(nw, wgu, wd, rank, world, EPS, kind="dot", exchange=ex)(x)
+                outs.append(_np(x))
+            res.append(np.stack(outs))
         torch.cuda.synchronize()
-        np.save(os.path.join(outdir, f"rank{rank}.npy"), _np(x))
+        np.save(os.path.join(outdir, f"rank{rank}.npy"), np.stack(res))  # [mode, layer, m, h]
     finally:
         if ex is not None:
             ex.close()
@@ -252,11 +289,21 @@ def _rank_main_nvlink(rank, world, port, outdir, h, i, m, layers):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_tp_nvlink_layers():
-    """Chained tensor-parallel layers with the NVLink exchange on 2..8 GPUs:
-    every rank ends with the same bits, equal to the unsharded oracle chain."""
+    """Chained tensor-parallel layers with the NVLink exchange on 2..8 GPUs,
+    the rank sum folded into the down projection and as its own kernel:
+    every rank ends with the same bits in both modes, equal to the unsharded
+    oracle chain.  h = 1024 splits the down projection stream-K, h = 4096 by
+    clusters."""
     import torch.multiprocessing as mp
 
-    h, i, m, layers = 1024, 2816, 4, 3
+    for h in (1024, 4096):
+        _nvlink_layers(h)
+
+
+def _nvlink_layers(h):
+    import torch.multiprocessing as mp
+
+    i, m, layers = 2816, 4, 3
     world = min(torch.cuda.device_count(), 8)
     while (i % world or (i // world) % 8) and world > 2:
         world -= 1
@@ -264,14 +311,15 @@ def test_tp_nvlink_layers():
         mp.start_processes(_rank_main_nvlink, args=(world, _free_port(), d, h, i, m, layers), nprocs=world,
                            join=True, start_method="spawn")
         outs = [np.load(os.path.join(d, f"rank{r}.npy")) for r in range(world)]
-    for o in outs[1:]:
-        assert np.array_equal(o, outs[0])
+    for o in outs:
+        assert np.array_equal(o[0], outs[0][0]) and np.array_equal(o[1], outs[0][0])
+    # every layer within the parity bar of the unsharded oracle on its own input
     x = None
     for layer in range(layers):
         x0, nw, wgu, wd = [_np(t) for t in _layer(h, i, m, 500 + layer, device="cpu")]
-        x = x0 if x is None else x
-        x = O.post_attn_mlp(x, nw, wgu, wd, EPS, "bfloat16")
-    torch.testing.assert_close(torch.from_numpy(outs[0]), torch.from_numpy(x), **TOL)
+        x = x0 if x is None else outs[0][0][layer - 1]
+        ref = O.post_attn_mlp(x, nw, wgu, wd, EPS, "bfloat16")
+        torch.testing.assert_close(torch.from_numpy(outs[0][0][layer]), torch.from_numpy(ref), **TOL)
 
 
 @pytest.mark.parametrize("m", [1, 8])
@@ -339,7 +387,7 @@ def _rank_main_tp_stack(rank, world, port, outdir, h, i, m, layers):
         out = torch.empty_like(x0)
         K.post_attn_mlp_tp_stack_out(x0, shards, out, EPS, "dot", ex)  # one persistent kernel
         x = x0
-        for nw, wgu, wd in shards:  # three launches per layer
+        for nw, wgu, wd in shards:  # two launches per layer
             x = tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)(x)
         stack = MlpStack(shards, m, EPS, kind="dot", exchange=ex)
         g = [stack(x0).clone() for _ in range(2)]
