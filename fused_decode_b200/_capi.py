@@ -128,6 +128,7 @@ SIGNATURES: dict[str, tuple] = {
         ],
     ),
     "fd_post_attn_mlp_stack_launches": (c_i32, [c_i32, c_i32, c_i32, c_i64, c_i64, c_i32]),
+    "fd_post_attn_mlp_layer_launches": (c_i32, [c_i32, c_i64, c_i64, c_i32, c_i32, c_i32]),
     "fd_post_attn_mlp_tp_stack_launches": (c_i32, [c_i32, c_i32, c_i32, c_i64, c_i64, c_i32]),
     "fd_post_attn_mlp_tp_stack_out": (
         c_i32,

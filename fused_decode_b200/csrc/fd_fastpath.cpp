@@ -26,6 +26,7 @@
 #include <torch/csrc/autograd/python_variable.h>
 #include <torch/csrc/utils/pybind.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -380,11 +381,14 @@ bool mlp_fusable(const at::Tensor& hidden, const at::Tensor& nw, const at::Tenso
   if (wgu.stride(1) != 1 || wd.stride(1) != 1 || wgu.stride(0) % 8 || wd.stride(0) % 8) return false;
   for (const at::Tensor* t : {&hidden, &nw, &wgu, &wd})
     if (reinterpret_cast<uintptr_t>(t->data_ptr()) % 16) return false;
+  // the gate/up kernel's smallest ring (2 stages) with the resident or the
+  // streamed batch (kernels.mlp_fusable)
   const int64_t ks = (h + 127) / 128;
   const int64_t nes = nw.scalar_type() == at::kFloat ? 4 : 2;
-  const int64_t region = ks * 2 * m * 128 + ((h * nes + 15) & ~int64_t{15});
-  const int64_t smem = 1024 + 2 * 32768 + region + 64 * 16 * 4 + 2 * 12 * 8;
-  return smem <= 227 * 1024 - 1024;
+  const int64_t fixed = 1024 + 2 * 32768 + 64 * 16 * 4 + 2 * 12 * 8;
+  const int64_t resident = fixed + ks * 2 * m * 128 + ((h * nes + 15) & ~int64_t{15});
+  const int64_t streamed = fixed + 2 * 2 * (m <= 8 ? 1024 : 2048);
+  return std::min(resident, streamed) <= 227 * 1024 - 1024;
 }
 
 py::object post_attn_mlp(py::handle hh, py::handle hnw, py::handle hgu, py::handle hd, py::handle heps,

@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
     grid_dep_wait();
     if (lane == 0) announce_mid(a, ms, s0, s1, G, &s_abort);
     __syncwarp();
-    if (MODE == MODE_GATEUP) watch_final_staged<NT>(a, ms, s0, s1, G, c, r.fin);
+    if (gateup_mode(MODE)) watch_final_staged<NT>(a, ms, s0, s1, G, c, r.fin);
     grid_dep_launch();
     return;
   }
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
         bulk_load(nw_smem, a.norm_w, nb, &s_nw_bar);
       }
       prefetch_map(&wmap);
-      if (linear_mode(MODE)) prefetch_map(&xmap);
+      if (streams_x(MODE)) prefetch_map(&xmap);
       produce_phase<MODE>(r, &wmap, &xmap, a, s0, s1, 0, p, P, evict_first_policy(), &s_abort, [] {
         grid_dep_wait();  // the activation is the previous kernel's output
         return true;
@@ -89,6 +89,83 @@ __global__ void __launch_bounds__(MAXT, MINB)
   if (MODE == MODE_GATEUP) norm_to_smem<T>(a, a.hidden, r, s_sumsq, nw_smem, &s_nw_bar);
   grid_dep_launch();
   consume_phase<T, NT, KIND, MP, MODE>(a, r, s0, s1, 0, G, c, &s_last, &s_abort, ms);
+}
+
+// The gate/up stage's RMSNorm on its own, for the streamed gate/up mode: one
+// CTA of CONSUMERS threads per row writes normed[row] = round((x * scale) *
+// w) with norm_rows's arithmetic -- thread t sums the squares of vectors t,
+// t + CONSUMERS, ... as f32x2 pairs, then each warp, then the warps in
+// order; the same products -- so the bits equal the resident mode's
+// normalised batch.
+template <typename T>
+__global__ void __launch_bounds__(CONSUMERS) norm_rows_kernel(const GemvArgs a, T* __restrict__ normed) {
+  __shared__ float s_part[GW];
+  __shared__ float s_scale;
+  constexpr int VW = 4;  // vectors of a thread in flight (all of them for k <= 8192)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row = blockIdx.x;
+  const int nvec = static_cast<int>(a.k / 8);
+  grid_dep_wait();  // hidden is the previous kernel's output
+  grid_dep_launch();
+  const uint4* x = reinterpret_cast<const uint4*>(static_cast<const T*>(a.hidden) + row * a.hidden_stride);
+  uint4 raw[VW];
+  uint64_t acc = 0;  // {+0.f, +0.f}
+  for (int v0 = tid; v0 < nvec; v0 += VW * CONSUMERS) {
+#pragma unroll
+    for (int u = 0; u < VW; ++u) {
+      const int v = v0 + u * CONSUMERS;
+      raw[u] = v < nvec ? __ldcg(x + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < VW; ++u) {
+      if (v0 + u * CONSUMERS >= nvec) break;
+      const uint64_t p0 = pair_f32x2<T>(raw[u].x), p1 = pair_f32x2<T>(raw[u].y);
+      const uint64_t p2 = pair_f32x2<T>(raw[u].z), p3 = pair_f32x2<T>(raw[u].w);
+      acc = fma_f32x2(p0, p0, acc);
+      acc = fma_f32x2(p1, p1, acc);
+      acc = fma_f32x2(p2, p2, acc);
+      acc = fma_f32x2(p3, p3, acc);
+    }
+  }
+  const float2 hs = f32x2_split(acc);
+  const float t = warp_sum(hs.x + hs.y);
+  if (lane == 0) s_part[warp] = t;
+  __syncthreads();
+  if (tid == 0) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < GW; ++w) tot += s_part[w];
+    s_scale = rsqrtf(tot / static_cast<float>(a.k) + a.eps);
+  }
+  __syncthreads();
+  const uint64_t i2 = f32x2_of(s_scale, s_scale);
+  const int wes = a.norm_dtype == FD_F32 ? 4 : 2;
+  const unsigned char* nw = static_cast<const unsigned char*>(a.norm_w);
+  uint4* y = reinterpret_cast<uint4*>(normed + row * a.k);
+  const bool kept = nvec <= VW * CONSUMERS;  // every vector of this thread is still in raw[]
+#pragma unroll 1
+  for (int u = 0, v = tid; v < nvec; ++u, v += CONSUMERS) {
+    uint4 xv;
+    if (kept) {
+#pragma unroll
+      for (int uu = 0; uu < VW; ++uu)
+        if (uu == u) xv = raw[uu];
+    } else {
+      xv = __ldcg(x + v);
+    }
+    uint64_t w[4];
+    nw_pairs(nw + static_cast<int64_t>(v) * 8 * wes, a.norm_dtype, w);
+    const float2 o0 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(xv.x), i2), w[0]));
+    const float2 o1 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(xv.y), i2), w[1]));
+    const float2 o2 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(xv.z), i2), w[2]));
+    const float2 o3 = f32x2_split(mul_f32x2(mul_f32x2(pair_f32x2<T>(xv.w), i2), w[3]));
+    uint4 packed;
+    packed.x = pack2<T>(o0.x, o0.y);
+    packed.y = pack2<T>(o1.x, o1.y);
+    packed.z = pack2<T>(o2.x, o2.y);
+    packed.w = pack2<T>(o3.x, o3.y);
+    y[v] = packed;
+  }
 }
 
 // ------------------------------------------------------------ cluster split
@@ -433,14 +510,57 @@ int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvAr
 }
 
 // RMSNorm (prologue) -> gate/up GEMV -> SwiGLU -> mid [m, i].
+// Which gate/up mode a launch takes: the resident normalised batch (GATEUP:
+// the RMSNorm in the kernel's prologue) while it leaves the ring its full
+// depth; else the streamed batch (norm_rows_kernel, then GATEUP_S streaming
+// the normalised rows with the weights) -- one launch more, but a full ring
+// (8B widths above 10 rows, 70B widths above 4).  FD_GATEUP_STREAM = 1 / 0
+// forces one or the other (tests, tuning).
+struct GateUpPlan {
+  Geometry geo;
+  bool streamed;
+};
+
+GateUpPlan plan_gate_up(int m, int64_t h, int nes) {
+  const Geometry res = choose_geometry([m, h, nes](int, int boxes) {
+    const int64_t ks = (h + static_cast<int64_t>(boxes) * KC - 1) / (static_cast<int64_t>(boxes) * KC);
+    return gateup_region_bytes(m, ks, boxes, h, nes);
+  });
+  const Geometry str = choose_geometry([m](int stages, int boxes) { return linear_x_bytes(m, stages, boxes); });
+  const char* env = std::getenv("FD_GATEUP_STREAM");
+  if (env && env[0] == '1' && str.stages > 0) return {str, true};
+  if (env && env[0] == '0') return {res, false};
+  const Geometry full = choose_geometry([](int, int) { return size_t{0}; });  // the ring with no X region
+  if (res.stages >= full.stages || str.stages <= res.stages) return {res, false};
+  return {str, true};
+}
+
+}  // namespace
+
+namespace fd_host {
+int mlp_layer_launches(int32_t m, int64_t h, int64_t i, int32_t norm_dtype, int32_t kind, bool tensor_parallel) {
+  (void)i;
+  int n = plan_gate_up(m, h, norm_dtype == FD_F32 ? 4 : 2).streamed ? 3 : 2;
+  if (tensor_parallel && !(kind == FD_KIND_DOT && tp_fold_enabled())) ++n;
+  return n;
+}
+}  // namespace fd_host
+
+namespace {
+
+// MLP workspace tail: mid [m, i], two ping-pong hidden buffers [m, h], then
+// the streamed gate/up mode's normalised rows [m, h].
+char* normed_rows(const Workspace& ws, int m, int64_t h, int64_t i) {
+  const size_t mm = static_cast<size_t>(std::max(m, 1));
+  return ws.tail + align256(mm * i * 2) + 2 * align256(mm * h * 2);
+}
+
 int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, const void* w_gate_up,
                    int64_t s_gu, void* mid, int32_t dtype, int32_t m, int64_t h, int64_t i, float eps, int32_t kind,
                    const Workspace& ws, cudaStream_t st) {
   const int nes = norm_dtype == FD_F32 ? 4 : 2;
-  const Geometry geo = choose_geometry([m, h, nes](int, int boxes) {
-    const int64_t ks = (h + static_cast<int64_t>(boxes) * KC - 1) / (static_cast<int64_t>(boxes) * KC);
-    return gateup_region_bytes(m, ks, boxes, h, nes);
-  });
+  const GateUpPlan plan = plan_gate_up(m, h, nes);
+  const Geometry geo = plan.geo;
   if (geo.stages == 0) return FD_ERR_UNSUPPORTED;
   GemvArgs a = {};
   a.y = static_cast<char*>(mid); a.sym = i; a.syn = 1;
@@ -455,9 +575,23 @@ int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, c
   a.inner = i;
   a.hidden = hidden; a.hidden_stride = h;
   a.norm_w = norm_w; a.norm_dtype = norm_dtype; a.eps = eps;
-  CUtensorMap gm;
+  CUtensorMap gm, xm;
   if (!make_gate_up_map(&gm, w_gate_up, h, i, s_gu)) return FD_ERR_LAUNCH;
-  size_t smem = ring_smem_bytes(gateup_region_bytes(m, a.ks, a.boxes, h, nes), a.stages, a.boxes);
+  if (plan.streamed) {
+    // the normalised rows first, then [m x 64] boxes of them with each weight step
+    char* normed = normed_rows(ws, m, h, i);
+    if (!make_map_2d(&xm, normed, m, h, h, m)) return FD_ERR_LAUNCH;
+    const cudaError_t en =
+        dtype == FD_BF16
+            ? fd_host::launch_pdl(norm_rows_kernel<__nv_bfloat16>, dim3(m), CONSUMERS, 0, st, a,
+                                  reinterpret_cast<__nv_bfloat16*>(normed))
+            : fd_host::launch_pdl(norm_rows_kernel<__half>, dim3(m), CONSUMERS, 0, st, a, reinterpret_cast<__half*>(normed));
+    if (en != cudaSuccess) return FD_ERR_LAUNCH;
+  }
+  a.x_slot = plan.streamed ? x_slot_bytes(m) : 0;
+  size_t smem = ring_smem_bytes(plan.streamed ? linear_x_bytes(m, a.stages, a.boxes)
+                                              : gateup_region_bytes(m, a.ks, a.boxes, h, nes),
+                                a.stages, a.boxes);
   // room for the final block's staged partials (batches up to 8 rows), where
   // it costs no ring stage
   const size_t fin = fin_stage_bytes(1);
@@ -465,8 +599,13 @@ int launch_gate_up(const void* hidden, const void* norm_w, int32_t norm_dtype, c
     smem += fin;
     a.fin_stage = 1;
   }
-  cudaError_t e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st)
-                                   : dispatch_tma<__half, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st);
+  cudaError_t e;
+  if (plan.streamed)
+    e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP_S>(gm, xm, a, kind, geo, smem, st)
+                         : dispatch_tma<__half, MODE_GATEUP_S>(gm, xm, a, kind, geo, smem, st);
+  else
+    e = dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st)
+                         : dispatch_tma<__half, MODE_GATEUP>(gm, gm, a, kind, geo, smem, st);
   return from_cuda(e);
 }
 
@@ -487,10 +626,11 @@ int check_mlp_args(const void* hidden, const void* norm_w, int32_t norm_dtype, c
 }
 
 // MLP intermediates behind the stream-K workspace: mid [m, i], then two
-// ping-pong hidden buffers [m, h] for the layers of a stack.
+// ping-pong hidden buffers [m, h] for the layers of a stack, then the
+// streamed gate/up mode's normalised rows [m, h] (normed_rows).
 size_t mlp_tail_bytes(int m, int64_t h, int64_t i) {
   const size_t mm = static_cast<size_t>(std::max(m, 1));
-  return align256(mm * i * 2) + 2 * align256(mm * h * 2);
+  return align256(mm * i * 2) + 3 * align256(mm * h * 2);
 }
 
 // One post_attn_mlp layer as two launches on `st`: gate/up (RMSNorm prologue,
@@ -582,7 +722,7 @@ int fd_mlp_gate_up_out(const void* hidden, const void* norm_w, int32_t norm_dtyp
   if (chk != FD_OK) return chk;
   if (m == 0 || h == 0) return FD_OK;
   if (!mid) return FD_ERR_ARG;
-  if (!workspace || workspace_bytes < streamk_ws_bytes()) return FD_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < fd_post_attn_mlp_workspace_bytes(m, h, i)) return FD_ERR_WORKSPACE;
   return launch_gate_up(hidden, norm_w, norm_dtype, w_gate_up, s_gu, mid, dtype, m, h, i, eps, kind,
                         carve(workspace), static_cast<cudaStream_t>(stream));
 }

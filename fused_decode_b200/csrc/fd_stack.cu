@@ -525,7 +525,8 @@ int mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h,
   const bool persistent =
       kind == FD_KIND_DOT && m <= MT_MAX &&
       persistent_wanted(false, stack_geometry(m, h, i, norm_dtype == FD_F32 ? 4 : 2, sm_count()));
-  return persistent ? (layers + kStackMaxLayers - 1) / kStackMaxLayers : 2 * layers;
+  return persistent ? (layers + kStackMaxLayers - 1) / kStackMaxLayers
+                    : layers * mlp_layer_launches(m, h, i, norm_dtype, kind, false);
 }
 
 }  // namespace fd_host
@@ -537,7 +538,13 @@ extern "C" int fd_post_attn_mlp_tp_stack_launches(int32_t layers, int32_t norm_d
       kind == FD_KIND_DOT && m <= MT_MAX &&
       fd_host::persistent_wanted(true, stack_geometry(m, h, i, norm_dtype == FD_F32 ? 4 : 2, fd_host::sm_count()));
   if (persistent) return (layers + kStackMaxLayers - 1) / kStackMaxLayers;
-  return (kind == FD_KIND_DOT && fd_host::tp_fold_enabled() ? 2 : 3) * layers;
+  return layers * fd_host::mlp_layer_launches(m, h, i, norm_dtype, kind, true);
+}
+
+extern "C" int fd_post_attn_mlp_layer_launches(int32_t m, int64_t h, int64_t i, int32_t norm_dtype, int32_t kind,
+                                               int32_t tensor_parallel) {
+  if (m <= 0 || h <= 0) return 0;
+  return fd_host::mlp_layer_launches(m, h, i, norm_dtype, kind, tensor_parallel != 0);
 }
 
 extern "C" int fd_post_attn_mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,

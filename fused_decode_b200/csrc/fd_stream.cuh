@@ -67,9 +67,15 @@ constexpr int kStatusEmptyTimeout = 2;
 // projection: its activation is written inside the same kernel).
 // MODE_LINEAR_TP: LINEAR whose epilogue also sums the tensor-parallel ranks
 // (tp_fold_block) -- its own instantiations, so the plain LINEAR kernels
-// carry none of that code.
-enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2, MODE_LINEAR_TP = 3 };
+// carry none of that code.  MODE_GATEUP_S: GATEUP whose normalised batch was
+// written by norm_rows_kernel and streams in [m x 64] boxes by TMA with each
+// weight step, instead of being normalised into shared memory whole (which
+// leaves too few ring stages for wide or tall batches).
+enum Mode { MODE_LINEAR = 0, MODE_GATEUP = 1, MODE_LINEAR_X = 2, MODE_LINEAR_TP = 3, MODE_GATEUP_S = 4 };
 __host__ __device__ constexpr bool linear_mode(int mode) { return mode == MODE_LINEAR || mode == MODE_LINEAR_TP; }
+__host__ __device__ constexpr bool gateup_mode(int mode) { return mode == MODE_GATEUP || mode == MODE_GATEUP_S; }
+// activation boxes stream through per-stage slots with the weight boxes
+__host__ __device__ constexpr bool streams_x(int mode) { return linear_mode(mode) || mode == MODE_GATEUP_S; }
 
 // One phase of streaming: a GEMV (LINEAR) or the MLP gate/up stage (GATEUP).
 struct GemvArgs {
@@ -559,6 +565,10 @@ struct Epilogue<T, NT, MODE_GATEUP> {
   }
 };
 
+// GATEUP_S: the same epilogue (only the activation's path differs).
+template <typename T, int NT>
+struct Epilogue<T, NT, MODE_GATEUP_S> : Epilogue<T, NT, MODE_GATEUP> {};
+
 // Split-K bookkeeping.  A CTA's range [s0, s1) holds at most two blocks it
 // does not cover whole: the block it starts inside (slot 0) and the block it
 // ends inside (slot 1).  Their partials go to the CTA's two slots with plain
@@ -835,8 +845,8 @@ FD_DEV void announce_mid(const GemvArgs& a, const MidSync& ms, int64_t s0, int64
 // Shared-memory layout (1024-byte aligned base):
 //   [W ring: S x B x 16 KB][X region][xchg: 64 x 16 floats][full[12]][empty[12]]
 //   [fin: GATEUP launches with fin_stage, kFinOthers x BR x 8 * NT floats]
-// X region: LINEAR activation boxes (S x B x x_slot), or the GATEUP normalised
-// batch (ks x B chunks of [m x 128 B]).
+// X region: LINEAR and GATEUP_S activation boxes (S x B x x_slot), or the
+// GATEUP normalised batch (ks x B chunks of [m x 128 B]).
 struct Ring {
   unsigned char* wst;
   unsigned char* xreg;
@@ -875,7 +885,7 @@ FD_DEV void ring_init(const Ring& r) {
 
 template <int MODE>
 FD_DEV uint32_t stage_bytes(const Ring& r, const GemvArgs& a) {
-  return static_cast<uint32_t>(r.w_stage) + (linear_mode(MODE) ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
+  return static_cast<uint32_t>(r.w_stage) + (streams_x(MODE) ? static_cast<uint32_t>(r.B * a.m * 128) : 0u);
 }
 
 // Weight boxes of phase step t into ring index gi.
@@ -886,7 +896,7 @@ FD_DEV void issue_w(const Ring& r, const CUtensorMap* map, const GemvArgs& a, in
   unsigned char* dst = r.wst + s * r.w_stage;
   for (int j = 0; j < r.B; ++j) {
     const int32_t col = static_cast<int32_t>((kk * r.B + j) * KC);
-    if (MODE == MODE_GATEUP)
+    if (gateup_mode(MODE))
       tma_load_3d(dst + j * BOX_BYTES, map, col, static_cast<int32_t>(b * (BR / 2)), 0, &r.full[s], pol);
     else
       tma_load_2d(dst + j * BOX_BYTES, map, col, static_cast<int32_t>(b * BR), &r.full[s], pol);
@@ -931,7 +941,7 @@ FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensor
     mbar_expect_tx(&r.full[gi % r.S], sb);
     issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
   }
-  if (linear_mode(MODE)) {
+  if (streams_x(MODE)) {
     if (!ready()) return false;
     for (int64_t g2 = first; g2 < base + npre; g2 += P) issue_x(r, xmap, a, s0 + (g2 - base), g2);
   }
@@ -939,7 +949,7 @@ FD_DEV bool produce_phase(const Ring& r, const CUtensorMap* wmap, const CUtensor
     if (!acquire(gi)) return false;
     mbar_expect_tx(&r.full[gi % r.S], sb);
     issue_w<MODE>(r, wmap, a, s0 + (gi - base), gi, pol);
-    if (linear_mode(MODE)) issue_x(r, xmap, a, s0 + (gi - base), gi);
+    if (streams_x(MODE)) issue_x(r, xmap, a, s0 + (gi - base), gi);
   }
   return true;
 }
@@ -1204,7 +1214,7 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
     }
     // activation box j of this step: [m rows x 128 B] (swizzled by row & 7)
     auto xbox = [&](int j) -> const unsigned char* {
-      if (linear_mode(MODE)) return r.xreg + (s * B + j) * r.x_slot;
+      if (streams_x(MODE)) return r.xreg + (s * B + j) * r.x_slot;
       if (MODE == MODE_LINEAR_X) return r.xreg + ((it * B + j) * a.m) * 128;
       return r.xreg + ((ck * B + j) * a.m) * 128;
     };
@@ -1315,7 +1325,7 @@ FD_DEV bool consume_phase(const GemvArgs& a, const Ring& r, int64_t s0, int64_t 
         write_slot<NT>(a, 0, acc, c);
         __syncwarp();
         if (lane == 0) mbar_arrive(ms.ready);
-      } else if (MODE == MODE_GATEUP && head_of_final(s0, s1, a.ks)) {
+      } else if (gateup_mode(MODE) && head_of_final(s0, s1, a.ks)) {
         Acc<NT> ex;
         Epilogue<T, NT, MODE>::extras(a, cb, ex);
         if (threadIdx.x == 0) {
@@ -1442,13 +1452,17 @@ __host__ __device__ inline int x_slot_bytes(int m) { return m <= 8 ? 1024 : 2048
 __host__ __device__ inline size_t gateup_x_bytes(int m, int64_t ks, int boxes) {
   return static_cast<size_t>(ks) * boxes * m * 128;
 }
+__host__ __device__ inline size_t nw_copy_bytes(int64_t k, int norm_es) {
+  return (static_cast<size_t>(k) * norm_es + 15) & ~static_cast<size_t>(15);
+}
 // The gate/up X region: the normalised batch, then the norm weight's copy.
 __host__ __device__ inline size_t gateup_region_bytes(int m, int64_t ks, int boxes, int64_t k, int norm_es) {
-  return gateup_x_bytes(m, ks, boxes) + ((static_cast<size_t>(k) * norm_es + 15) & ~static_cast<size_t>(15));
+  return gateup_x_bytes(m, ks, boxes) + nw_copy_bytes(k, norm_es);
 }
 __host__ __device__ inline size_t linear_x_bytes(int m, int stages, int boxes) {
   return static_cast<size_t>(stages) * boxes * x_slot_bytes(m);
 }
+
 inline size_t ring_smem_bytes(size_t xbytes, int stages, int boxes) {
   return 1024 + static_cast<size_t>(stages) * boxes * BOX_BYTES + ((xbytes + 15) & ~static_cast<size_t>(15)) +
          (BR / 2) * MT_MAX * 4 + 2 * MAX_STAGES * 8;
@@ -1498,6 +1512,9 @@ int mlp_stack_persistent(const void* hidden, int32_t layers, const void* const* 
                          int32_t tp_rank = 0, int32_t tp_world = 0, void* const* exchange = nullptr,
                          int32_t tp_mmax = 0);
 int mlp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i, int32_t kind);
+// Kernel launches of one post_attn_mlp layer (fd_gemv.cu): gate/up (+ the
+// streamed mode's norm kernel), down (+ the tensor-parallel reduce kernel).
+int mlp_layer_launches(int32_t m, int64_t h, int64_t i, int32_t norm_dtype, int32_t kind, bool tensor_parallel);
 
 // Tensor parallel: with FD_TP_FOLD=1 (and kind = dot) the rank sum runs in
 // the down projection's epilogue (tp_fold_block, two launches a layer);

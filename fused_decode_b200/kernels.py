@@ -283,13 +283,16 @@ def mlp_fusable(hidden2: torch.Tensor, norm_weight: torch.Tensor, w_gate_up: tor
         if t.data_ptr() % 16:
             return False
     # Shared memory of the gate/up kernel with its smallest ring (2 stages of
-    # 32 KB): the RMSNorm'd batch (h padded to 128 columns) and a copy of the
-    # norm weight (fd_stream.cuh: ring_smem_bytes, gateup_region_bytes).
+    # 32 KB) in either mode: the RMSNorm'd batch (h padded to 128 columns)
+    # and a copy of the norm weight, or the streamed normalised batch's 2 x 2
+    # box slots (fd_stream.cuh: ring_smem_bytes, gateup_region_bytes,
+    # linear_x_bytes).
     ks = -(-h // 128)
     nes = 4 if norm_weight.dtype == torch.float32 else 2
-    region = ks * 2 * m * 128 + ((h * nes + 15) & ~15)
-    smem = 1024 + 2 * 32768 + region + 64 * 16 * 4 + 2 * 12 * 8
-    return smem <= 227 * 1024 - 1024
+    fixed = 1024 + 2 * 32768 + 64 * 16 * 4 + 2 * 12 * 8
+    resident = fixed + ks * 2 * m * 128 + ((h * nes + 15) & ~15)
+    streamed = fixed + 2 * 2 * (1024 if m <= 8 else 2048)
+    return min(resident, streamed) <= 227 * 1024 - 1024
 
 
 def post_attn_mlp_out(

@@ -102,12 +102,16 @@ class MlpStack:
     @property
     def launches_per_replay(self) -> int:
         """Kernel launches of this library per replay: one persistent kernel
-        per 32 layers where the stack entry point runs one, else two per layer
-        (three per layer for a tensor-parallel stack)."""
-        per_layer = 3 if self.exchange is not None else 2
-        if not self.fused:
-            return per_layer * len(self.layers)
+        per 32 layers where the stack entry point runs one, else the layer's
+        launches (two; a third where the gate/up stage streams the normalised
+        rows; another for the tensor-parallel rank sum) per layer."""
         nw0, wgu0, wd0 = self.layers[0]
+        if not self.fused:
+            per_layer = _capi.load().fd_post_attn_mlp_layer_launches(
+                int(self.static_in.shape[0]), self.h, int(wd0.shape[1]), _capi.dtype_code(nw0.dtype),
+                _capi.FD_KIND_DOT if self.kind == "dot" else _capi.FD_KIND_SIMT,
+                1 if self.exchange is not None else 0)
+            return int(per_layer) * len(self.layers)
         if self.exchange is not None:
             return int(_capi.load().fd_post_attn_mlp_tp_stack_launches(
                 len(self.layers), _capi.dtype_code(nw0.dtype), int(self.static_in.shape[0]), self.h,

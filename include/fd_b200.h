@@ -258,6 +258,13 @@ int fd_post_attn_mlp_tp_out(const void* hidden, const void* norm_w, int32_t norm
  * per-layer launches on 2 B200s, so not the default).  The same exchange and
  * round-counting rules as
  * fd_post_attn_mlp_tp_out.  Workspace: fd_post_attn_mlp_workspace_bytes(m, h, i). */
+/* Kernel launches of one fd_post_attn_mlp_out (tensor_parallel = 0) or
+ * fd_post_attn_mlp_tp_out (1) call of this shape (no counterpart in the
+ * reference): two, plus a norm kernel where the gate/up stage streams the
+ * normalised rows (batches whose normalised rows would leave its shared-memory
+ * ring shallow), plus the rank-sum kernel for tensor parallel. */
+int fd_post_attn_mlp_layer_launches(int32_t m, int64_t h, int64_t i, int32_t norm_dtype, int32_t kind,
+                                    int32_t tensor_parallel);
 /* Kernel launches one fd_post_attn_mlp_tp_stack_out call of this shape makes
  * (i: this rank's share of the intermediate width). */
 int fd_post_attn_mlp_tp_stack_launches(int32_t layers, int32_t norm_dtype, int32_t m, int64_t h, int64_t i,

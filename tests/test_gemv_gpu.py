@@ -346,11 +346,11 @@ def test_persistent_stack_two_launches(monkeypatch):
         assert torch.equal(out, x)
 
 
-@pytest.mark.parametrize("m", [1, 8])
+@pytest.mark.parametrize("m", [1, 8, 16])
 def test_post_attn_mlp_llama70b_widths(m):
     """Llama-3-70B widths (hidden 8192, intermediate 28672) through the fused
-    two-kernel MLP, up to the batch where the gate/up stage's resident
-    normalised batch still fits its shared memory (8 rows).
+    two-kernel MLP at every batch: M = 1 and 8 hold the normalised batch in
+    shared memory, M = 16 streams it (the resident batch would not fit).
 
     Tolerance: the reference's own for its linear paths in bf16 (rtol = atol =
     4e-2, its tests/test_ops.py:27-35).  The reference rounds gate_up and mid
@@ -371,6 +371,63 @@ def test_post_attn_mlp_llama70b_widths(m):
         mid = torch.empty(m, i, device="cuda", dtype=dtype)
         K.mlp_gate_up_out(x, nw, wgu, mid, 1e-5, kind)
         _close(y, O.linear(_np(mid), _np(wd), row_add=_np(x), dtype="bfloat16"))
+
+
+@pytest.mark.parametrize("norm_f32", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("h", [1032, 4096])
+@pytest.mark.parametrize("m", [1, 3, 8, 16])
+def test_gate_up_streamed_matches_resident(m, h, dtype, norm_f32, monkeypatch):
+    """The gate/up stage with the normalised batch streamed (norm_rows_kernel
+    writes it, [m x 64] boxes arrive by TMA with each weight step) gives the
+    same bits as with the whole normalised batch resident in shared memory,
+    for both consumer kinds, an fp32 norm weight, and a hidden width whose
+    last 64-column box is partial (1032); the full layer in the streamed mode
+    is within the parity bar of the oracle, and the status word stays clear."""
+    i = 2816
+    nw, wgu, wd = _mlp_weights(h, i, dtype, 1300 + m)
+    if norm_f32:
+        nw = nw.float()
+    x = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(1350 + m))
+    for kind in ("dot", "simt"):
+        mids = {}
+        for mode in ("0", "1"):
+            monkeypatch.setenv("FD_GATEUP_STREAM", mode)
+            mid = torch.empty(m, i, device="cuda", dtype=dtype)
+            K.mlp_gate_up_out(x, nw, wgu, mid, 1e-5, kind)
+            mids[mode] = mid
+        assert torch.equal(mids["0"], mids["1"]), kind
+        monkeypatch.setenv("FD_GATEUP_STREAM", "1")
+        y = post_attn_mlp(x, nw, wgu, wd, 1e-5, kind=kind)
+        _close(y, O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), 1e-5, _NAME[dtype]))
+    torch.cuda.synchronize()
+    assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+
+
+@pytest.mark.parametrize("m", [8, 16])
+def test_gate_up_streamed_stack(m, monkeypatch):
+    """A 4-layer stack whose gate/up stages stream the batch (forced): the
+    stack entry point, per-layer calls and graph replays agree bit for bit,
+    run after run, three launches a layer."""
+    from fused_decode_b200.stack import MlpStack
+
+    monkeypatch.setenv("FD_GATEUP_STREAM", "1")
+    h, i, layers = 4096, 2816, 4
+    dtype = torch.bfloat16
+    ws = [_mlp_weights(h, i, dtype, 1400 + l) for l in range(layers)]
+    x0 = torch.randn(m, h, device="cuda", dtype=dtype, generator=_gen(1450 + m))
+    x = x0
+    for nw, wgu, wd in ws:
+        x = post_attn_mlp(x, nw, wgu, wd, kind="dot")
+    out = torch.empty_like(x0)
+    K.post_attn_mlp_stack_out(x0, ws, out, 1e-6, "dot")
+    assert torch.equal(out, x)
+    stack = MlpStack(ws, m, 1e-6, kind="dot")
+    assert stack.launches_per_replay == 3 * layers  # norm kernel, gate/up, down
+    for _ in range(3):
+        assert torch.equal(stack(x0), x)
+    torch.cuda.synchronize()
+    assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
 
 
 @pytest.mark.parametrize("m", [1, 8, 16])
