@@ -227,6 +227,37 @@ def test_tp_exchange_single_rank(m, h, fold, monkeypatch):
         ex.close()
 
 
+@pytest.mark.parametrize("fold", ["0", "1"])
+def test_tp_exchange_single_rank_streamed(fold, monkeypatch):
+    """A tensor-parallel layer (group of one) whose gate/up stage streams the
+    normalised rows (8 rows at 70B hidden width take that mode by default):
+    the same bits as post_attn_mlp, round after round, within the parity bar
+    of the oracle, four launches a layer with the reduce kernel."""
+    from fused_decode_b200 import kernels as K
+    from fused_decode_b200 import post_attn_mlp
+    from fused_decode_b200.stack import MlpStack
+
+    monkeypatch.setenv("FD_TP_FOLD", fold)
+    h, i, m = 8192, 2816, 8
+    ex = tp.TPExchange(h, m_max=16)
+    try:
+        layers = [_layer(h, i, m, 1500 + l)[1:] for l in range(2)]
+        x = _layer(h, i, m, 1550)[0]
+        for rnd in range(4):
+            nw, wgu, wd = layers[rnd % 2]
+            got = tp.TPPostAttnMlp(nw, wgu, wd, EPS, kind="dot", exchange=ex)(x)
+            assert torch.equal(got, post_attn_mlp(x, nw, wgu, wd, EPS, kind="dot")), rnd
+            ref = O.post_attn_mlp(_np(x), _np(nw), _np(wgu), _np(wd), EPS, "bfloat16")
+            torch.testing.assert_close(got.float().cpu(), torch.from_numpy(ref), **TOL)
+            x = got
+        per_layer = 3 if fold == "1" else 4
+        assert MlpStack(layers, m, EPS, kind="dot", exchange=ex).launches_per_replay == per_layer * len(layers)
+        torch.cuda.synchronize()
+        assert all(v == 0 for v in K.WORKSPACES.status().values()), K.WORKSPACES.status()
+    finally:
+        ex.close()
+
+
 @pytest.mark.parametrize("m", [1, 8])
 def test_tp_exchange_modes_interleaved(m, monkeypatch):
     """Layers alternating between the folded rank sum and the separate reduce
@@ -270,8 +301,11 @@ def _rank_main_nvlink(rank, world, port, outdir, h, i, m, layers):
         dev = torch.device("cuda", rank)
         ex = tp.TPExchange(h, m_max=16)
         res = []
-        for fold in ("1", "0"):  # rank sum in the down epilogue, then as its own kernel
+        # rank sum in the down epilogue, then as its own kernel; then with the
+        # gate/up stage streaming the normalised rows
+        for fold, stream in (("1", "0"), ("0", "0"), ("0", "1")):
             os.environ["FD_TP_FOLD"] = fold
+            os.environ["FD_GATEUP_STREAM"] = stream
             x, outs = None, []
             for layer in range(layers):
                 x0, nw, wgu, wd = _layer(h, i, m, 500 + layer, device=dev)
@@ -290,9 +324,10 @@ def _rank_main_nvlink(rank, world, port, outdir, h, i, m, layers):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_tp_nvlink_layers():
     """Chained tensor-parallel layers with the NVLink exchange on 2..8 GPUs,
-    the rank sum folded into the down projection and as its own kernel:
-    every rank ends with the same bits in both modes, equal to the unsharded
-    oracle chain.  h = 1024 splits the down projection stream-K, h = 4096 by
+    the rank sum folded into the down projection and as its own kernel, and
+    the gate/up stage streaming the normalised rows: every rank ends with the
+    same bits in every mode, each layer within the parity bar of the
+    unsharded oracle on its own input.  h = 1024 splits the down projection stream-K, h = 4096 by
     clusters."""
     import torch.multiprocessing as mp
 
@@ -312,7 +347,8 @@ def _nvlink_layers(h):
                            join=True, start_method="spawn")
         outs = [np.load(os.path.join(d, f"rank{r}.npy")) for r in range(world)]
     for o in outs:
-        assert np.array_equal(o[0], outs[0][0]) and np.array_equal(o[1], outs[0][0])
+        for mode in range(o.shape[0]):
+            assert np.array_equal(o[mode], outs[0][0]), mode
     # every layer within the parity bar of the unsharded oracle on its own input
     x = None
     for layer in range(layers):
