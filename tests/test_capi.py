@@ -111,3 +111,39 @@ def test_direct_copy_and_triad():
     dst = torch.zeros(1001, device="cuda", dtype=torch.uint8)
     K.launch_copy(dst[1:], src[1:])
     assert torch.equal(dst[1:], src[1:])
+
+
+def test_layer_launch_counts_without_gpu(monkeypatch):
+    """Kernel launches one post_attn_mlp layer enqueues -- a host-side plan,
+    so no GPU is needed: two (gate/up, down); three where the gate/up stage
+    streams the normalised rows because the resident batch would leave its
+    shared-memory ring under 4 stages (8B hidden width above 10 rows, 9 with
+    an fp32 norm weight; 70B hidden width above 4); one more for the
+    tensor-parallel rank sum, unless FD_TP_FOLD=1 folds it into the down
+    projection (dot consumers only).  FD_GATEUP_STREAM forces either mode."""
+    import torch
+
+    from fused_decode_b200 import _capi
+
+    lib = _capi.load()
+    bf, f32 = _capi.dtype_code(torch.bfloat16), _capi.dtype_code(torch.float32)
+    dot, simt = _capi.FD_KIND_DOT, _capi.FD_KIND_SIMT
+    monkeypatch.delenv("FD_GATEUP_STREAM", raising=False)
+    monkeypatch.delenv("FD_TP_FOLD", raising=False)
+
+    def n(m, h, nd=bf, kind=dot, tp=0):
+        return lib.fd_post_attn_mlp_layer_launches(m, h, 14336, nd, kind, tp)
+
+    assert [n(m, 4096) for m in (1, 8, 10, 11, 16)] == [2, 2, 2, 3, 3]
+    assert [n(m, 4096, nd=f32) for m in (9, 10)] == [2, 3]
+    assert [n(m, 8192) for m in (1, 4, 5, 8, 16)] == [2, 2, 3, 3, 3]
+    assert n(1, 4096, tp=1) == 3 and n(8, 8192, tp=1) == 4
+    monkeypatch.setenv("FD_TP_FOLD", "1")
+    assert n(1, 4096, tp=1) == 2 and n(8, 8192, tp=1) == 3
+    assert n(1, 4096, kind=simt, tp=1) == 3  # the fold has dot instantiations only
+    monkeypatch.delenv("FD_TP_FOLD")
+    monkeypatch.setenv("FD_GATEUP_STREAM", "1")
+    assert n(1, 4096) == 3
+    monkeypatch.setenv("FD_GATEUP_STREAM", "0")
+    assert n(16, 4096) == 2
+    assert n(0, 4096) == 0
