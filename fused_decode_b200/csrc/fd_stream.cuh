@@ -115,8 +115,9 @@ struct GemvArgs {
   int64_t tp_data_off;
   const int* tp_seq;  // this rank's round number
   // cluster split (gemv_cluster_kernel): each block's K steps are divided
-  // among cl_split CTAs of one thread-block cluster
-  int32_t cl_split;
+  // among cl_split CTAs of one thread-block cluster, whose rings are filled
+  // by cl_producers producer warps
+  int32_t cl_split, cl_producers;
   // GATEUP stream-K: shared memory after the ring holds the final block's
   // later contributors' partials, staged by the announcer warp (fin_stage_ok)
   int32_t fin_stage;
