@@ -1485,15 +1485,21 @@ struct Geometry {
 template <typename XBytes>
 Geometry choose_geometry(XBytes xbytes) {
   Geometry g{2, 2, 4};
+  bool tuned = false;
   if (const char* env = std::getenv("FD_GEMV_GEOMETRY")) {  // tuning override: "producers,boxes,stages"
     int b = 0, c = 0, d = 0;
     if (std::sscanf(env, "%d,%d,%d", &b, &c, &d) == 3 && b >= 1 && b <= MAX_PRODUCERS && c >= 1 &&
-        c <= MAX_BOXES && d >= 2 && d <= MAX_STAGES)
+        c <= MAX_BOXES && d >= 2 && d <= MAX_STAGES) {
       g = {b, c, d};
+      tuned = true;
+    }
   }
   auto bytes = [&](int st) { return ring_smem_bytes(xbytes(st, g.boxes), st, g.boxes); };
   while (g.stages > 2 && bytes(g.stages) > kSmemPerCta) --g.stages;
-  g.stages -= g.stages % g.producers;  // every stage is always refilled by the same producer
+  // By default every stage is refilled by the same producer; an override may
+  // give any stage count (producers then alternate on a stage, which is
+  // correct: each waits for its own index's stage to be released).
+  if (!tuned) g.stages -= g.stages % g.producers;
   if (g.stages < 2 || bytes(g.stages) > kSmemPerCta) g.stages = 0;
   return g;
 }
