@@ -523,6 +523,13 @@ int launch_linear(const void* x, int64_t sxm, const void* w, int64_t swn, GemvAr
     a.cl_split = 0;
     a.stages = geo.stages;
   }
+  // Stream-K: 5 stages under the same rule as the cluster kernel's ring
+  // (measured on B200, same call: N = 28672 K = 4096 40.4 -> 39.2 us at M = 1,
+  // 39.4 -> 38.9 at M = 8; N = 14336 -0.2 to -0.3 us; at M = 16 0.5 us slower).
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(fd_host::sm_count(), a.total));
+  if (a.m <= 8 && geo.stages == 4 && geo.producers == 2 && a.total / grid >= 16 && !std::getenv("FD_GEMV_GEOMETRY") &&
+      ring_smem_bytes(linear_x_bytes(a.m, 5, a.boxes), 5, a.boxes) <= kSmemPerCta)
+    a.stages = 5;
   const size_t smem = ring_smem_bytes(linear_x_bytes(a.m, a.stages, a.boxes), a.stages, a.boxes);
   cudaError_t e = tp_fold ? (dtype == FD_BF16 ? dispatch_tma<__nv_bfloat16, MODE_LINEAR_TP>(wm, xm, a, kind, geo, smem, st)
                                               : dispatch_tma<__half, MODE_LINEAR_TP>(wm, xm, a, kind, geo, smem, st))
